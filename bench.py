@@ -1,0 +1,393 @@
+"""Benchmark of the B200 video-DiT FFN stack (WAMInfer's hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE metric "FFN-stack ms/request and TFLOP/s (2F, 32/120 reuse)"):
+one step = R requests per GPU; one request = the FFN stack of one observation
+under the 2F schedule with 32/120 token reuse -- 30 layers at update 0 (layer 0
+over all 392 rows, layers 1..29 over 32 selected + 240 future + 32 action rows
+with cache scatter) and 30 layers at update 3 over all 392 rows.  d = 3072,
+hidden = 14336, tanh-GELU, seeded synthetic weights and activations.
+Requests are independent: with N GPUs each rank runs its own R requests (weak
+scaling, no data-path collective; one all-reduce of the elapsed time only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FFN-stack ms/request and TFLOP/s (2F, 32/120 reuse) at 1/2/4/8 B200; % bf16 roofline"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# dram__bytes_read.sum + dram__bytes_write.sum of one up-projection launch at
+# M = 392 from the committed ncu capture (profiles/umma_gemm_up_m392.md); None until captured.
+UP_GEMM_DRAM_BYTES = None
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--requests", type=int, default=8, help="requests per GPU per step")
+    p.add_argument("--layers", type=int, default=30)
+    p.add_argument("--cpu-sample-layers", type=int, default=2)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {k: float(data[k]) for k in FALLBACK_PEAKS}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL, start_new_session=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            try:
+                os.killpg(self.proc.pid, signal.SIGTERM)
+            except Exception:
+                pass
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if self.uuid and self.uuid not in parts[1]:
+                continue
+            rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU side
+def cpu_baseline(geo, sample_layers: int):
+    """The reference's native CPU FFN path (Linear -> GELU(tanh) -> Linear in
+    bf16, gather/scatter/gate in torch) restated by the oracle, timed on all
+    host cores over a bounded sample: `sample_layers` reuse layers (M = 304)
+    and `sample_layers` full-refresh layers (M = 392)."""
+    from oracle import cpu_path
+    from waminfer_b200.stack import ffn_flops
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    flops, seconds = cpu_path.time_layers(geo, sample_layers)
+    per_request_s = seconds / flops * geo.request_flops()
+    return {
+        "value": flops / seconds / 1e12,
+        "unit": "TFLOP/s",
+        "cores": threads,
+        "kind": "port",
+        "ms_per_request": per_request_s * 1e3,
+        "sample": f"{sample_layers} reuse layers (M={geo.reuse_rows}) + {sample_layers} full layers (M={geo.seq}) "
+                  f"of one request, bf16 torch CPU GEMMs, scaled to a request by FLOPs "
+                  f"({ffn_flops(geo.reuse_rows, geo.d, geo.h) * sample_layers / 1e12:.2f}+"
+                  f"{ffn_flops(geo.seq, geo.d, geo.h) * sample_layers / 1e12:.2f} TFLOP timed)",
+    }
+
+
+def run_reference(args, world, rank):
+    from waminfer_b200.stack import Geometry
+
+    if rank != 0:
+        return
+    geo = Geometry(layers=args.layers)
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_baseline(geo, 1)
+    values = []
+    for _ in range(args.steps):
+        values.append(cpu_baseline(geo, args.cpu_sample_layers))
+    value = statistics.median(v["value"] for v in values)
+    base = values[0]
+    ms = geo.request_flops() / (value * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "ms_per_request": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": config_dict(geo, args, world),
+        "cpu_baseline": {**base, "value": value},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(geo, args, world):
+    return {
+        "workload": "c4-request: 2F schedule, 32/120 token reuse, 30-layer FFN stack",
+        "layers": geo.layers, "d_model": geo.d, "d_hidden": geo.h,
+        "rows_update0": [geo.seq] + [geo.reuse_rows] * (geo.layers - 1), "rows_update3": geo.seq,
+        "requests_per_gpu_per_step": args.requests, "requests_per_step": args.requests * world,
+        "parallelism": f"request-parallel x{world}",
+        "l2": "no flush needed: each pass streams 30 x 176 MB of weights through the 126 MB L2",
+    }
+
+
+# ------------------------------------------------------------------ GPU side
+def time_dominant_kernel(device, geo, pk):
+    """CUDA-event timing of the up-projection GEMM (M = 392) launched alone:
+    achieved TFLOP/s against the burst bf16 peak."""
+    from waminfer_b200.ffn import Plan
+
+    g = torch.Generator(device=device).manual_seed(77)
+    m = geo.seq
+    x = (torch.randn(m, geo.d, device=device, generator=g)).to(torch.bfloat16)
+    w = (torch.randn(geo.h, geo.d, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    b = torch.zeros(geo.h, device=device, dtype=torch.bfloat16)
+    plan = Plan(x, w, b, exhaustive=False, gelu=True)
+    # Rotate over weight copies larger than L2 so every launch streams from HBM.
+    ws = [w] + [w.clone() for _ in range(3)]
+    stream = torch.cuda.current_stream(device)
+    for i in range(3):
+        plan.run(x, ws[i % 4], b)
+    iters = 40
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(device)
+    start.record(stream)
+    for i in range(iters):
+        plan.run(x, ws[i % 4], b)
+    end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / iters
+    flops = 2 * m * geo.d * geo.h
+    achieved = flops / (ms * 1e-3) / 1e12
+    plan.close()
+    del ws
+    return {
+        "kernel": "umma_gemm_kernel (up projection + bias + GELU, M=392)",
+        "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+        "frac": achieved / pk["bf16_tflops"], "us_per_launch": ms * 1e3,
+        "traffic": UP_GEMM_DRAM_BYTES,
+        "algorithmic_bytes": 2 * (geo.h * geo.d + m * geo.d + m * geo.h),
+    }
+
+
+def request_roofline_ms(geo, pk):
+    """Sum over layer passes of max(FLOPs / bf16 peak, bytes / HBM bandwidth)."""
+    total = 0.0
+    for m in geo.request_rows():
+        flops = 4 * m * geo.d * geo.h
+        bytes_ = 2 * geo.d * geo.h * 2 + 2 * m * geo.d * 2 + 2 * m * geo.h * 2 + 2 * m * geo.d * 2
+        total += max(flops / (pk["bf16_tflops_sustained"] * 1e12), bytes_ / (pk["hbm_gbs"] * 1e9))
+    return total * 1e3
+
+
+def run_ours(args, world, rank, local):
+    from waminfer_b200 import _lib
+    from waminfer_b200.stack import FFNStack, Geometry, Request, make_weights
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk, pk_kind = peaks()
+    geo = Geometry(layers=args.layers)
+    weights = make_weights(geo.layers, geo.d, geo.h, device, seed=0)
+    stack = FFNStack(weights, geo, device)
+    history = None
+    requests = []
+    for i in range(args.requests):
+        req = Request(geo, device, seed=rank * 100_000 + i, history_in=history)
+        requests.append(req)
+    stream = torch.cuda.Stream(device)
+    handle = stream.cuda_stream
+
+    # Eager warm-up (also checks the device status word), then capture R requests.
+    with torch.cuda.stream(stream):
+        for req in requests:
+            stack.enqueue_request(req, handle)
+    torch.cuda.synchronize(device)
+    status = stack.plan.status()
+    if status:
+        raise RuntimeError(f"device status {status:#x} after warm-up")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for req in requests:
+            stack.enqueue_request(req, handle)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        pass
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with Clocks(uuid) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms_step_local = start.elapsed_time(end) / args.steps
+    ms_step = max_over_ranks(ms_step_local, world, device)
+    flops_step = geo.request_flops() * args.requests * world
+    value = flops_step / (ms_step * 1e-3) / 1e12
+    ms_request = ms_step / args.requests
+    clk = clocks.summary()
+
+    # End to end: pinned host inputs -> device, graph replay, outputs -> host.
+    e2e = None
+    if not args.no_e2e:
+        host_in = [[r.x[0].cpu().pin_memory(), r.x[1].cpu().pin_memory(), r.indices.cpu().pin_memory()]
+                   for r in requests]
+        host_out = [[torch.empty_like(r.out[0], device="cpu").pin_memory() for _ in range(2)] for r in requests]
+        h2d = sum(t.numel() * t.element_size() for hs in host_in for t in hs)
+        d2h = sum(t.numel() * t.element_size() for hs in host_out for t in hs)
+
+        def e2e_step():
+            with torch.cuda.stream(stream):
+                for r, hi in zip(requests, host_in):
+                    r.x[0].copy_(hi[0], non_blocking=True)
+                    r.x[1].copy_(hi[1], non_blocking=True)
+                    r.indices.copy_(hi[2], non_blocking=True)
+                graph.replay()
+                for r, ho in zip(requests, host_out):
+                    ho[0].copy_(r.out[0], non_blocking=True)
+                    ho[1].copy_(r.out[1], non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize(device)
+        barrier(world)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e2.record(stream)
+        e2.synchronize()
+        barrier(world)
+        ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps, world, device)
+        e2e = {"value": flops_step / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
+               "ms_per_request": ms_e2e / args.requests, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    roof = time_dominant_kernel(device, geo, pk)
+    roof["peak_kind"] = f"{pk_kind} (burst bf16 GEMM)"
+    roof_ms = request_roofline_ms(geo, pk)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(geo, args.cpu_sample_layers)
+
+    launches = stack.launches_per_request() * args.requests * args.steps
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "ms_per_request": ms_request,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": config_dict(geo, args, world),
+            "request_roofline_ms": roof_ms, "request_roofline_frac": roof_ms / ms_request,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": launches, "launches_per_request": stack.launches_per_request(),
+            "library_launches_total": _lib.launch_count(),
+        }
+        print(json.dumps(line), flush=True)
+    graph.reset()
+    stack.close()
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            barrier(world)
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

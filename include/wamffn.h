@@ -1,0 +1,226 @@
+/*
+ * wamffn.h -- C ABI of the B200 (sm_100a) FFN hot path of WAMInfer's video DiT.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), returns an int status (WAMFFN_OK == 0) and never throws.
+ * On failure wamffn_last_error() returns a thread-local message.  No entry
+ * point allocates device memory or synchronises the stream except the
+ * *_create / *_destroy / *_tune / wamffn_*_status calls, so every run call can
+ * be captured into a CUDA graph (the reference forbids tuning during capture,
+ * _cublaslt_inference.cpp:167-168; *_create here refuses the same way).
+ *
+ * Tensors are bf16 (uint16 storage), row-major, last dimension contiguous.
+ * Weights use torch.nn.Linear's native [out_features, in_features] layout.
+ *
+ * Reference interfaces replaced (paths inside the WAMInfer project):
+ *   wamffn_linear_plan_create   <- Plan::Plan(x, weight, bias, exhaustive, gelu)
+ *                                  WAMInfer/_cublaslt_inference.cpp:161-174
+ *   wamffn_linear_run           <- Plan::run(x, weight, bias)
+ *                                  WAMInfer/_cublaslt_inference.cpp:177-188
+ *                                  (op wam_infer::prepared_ffn_linear_v1,
+ *                                   WAMInfer/ffn.py:38-45)
+ *   wamffn_linear_configuration <- Plan::selected_configuration()
+ *                                  WAMInfer/_cublaslt_inference.cpp:189
+ *   wamffn_ffn_run              <- PreparedFFN.forward(layer_id, inputs)
+ *                                  WAMInfer/ffn.py:96-107
+ *   wamffn_modulated_norm       <- op wam_infer::modulated_norm
+ *                                  WAMInfer/_triton_inference.py:130-221
+ *   wamffn_block_run            <- VideoAdapter post-attention norm + FFN phase:
+ *                                  WAMInfer/blocks.py:241-244 (CROSS_RESIDUAL norm),
+ *                                  WAMInfer/blocks.py:246-272 (gather, FFN,
+ *                                  cache scatter/concat, deferred gate) and the
+ *                                  FFN_RESIDUAL fold of
+ *                                  WAMInfer/_triton_inference.py:158-161
+ *   wamffn_select_tokens        <- select_tokens(state, features)
+ *                                  WAMInfer/approximation.py:55-67
+ */
+#ifndef WAMFFN_H
+#define WAMFFN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define WAMFFN_ABI_VERSION 1
+
+/* Status codes returned by every entry point. */
+#define WAMFFN_OK 0
+#define WAMFFN_ERR_INVALID 1     /* bad argument: shape, stride, alignment, null pointer */
+#define WAMFFN_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define WAMFFN_ERR_UNSUPPORTED 3 /* device is not sm_100 or geometry exceeds kernel limits */
+#define WAMFFN_ERR_CAPTURE 4     /* plan creation/tuning attempted during stream capture */
+#define WAMFFN_ERR_DEVICE 5      /* a kernel reported an error through the device status word */
+
+/* Bits of the device status word (wamffn_*_status). */
+#define WAMFFN_DEV_TIMEOUT 1u    /* a pipeline wait exceeded its time limit; the kernel bailed out */
+#define WAMFFN_DEV_BAD_INDEX 2u  /* a gather/scatter index was outside [-1, seq) or >= cache rows */
+
+/* Modes of wamffn_modulated_norm: the reference's MODE constants
+ * (WAMInfer/_triton_inference.py:117-120). */
+#define WAMFFN_SELF_INPUT 0
+#define WAMFFN_SELF_RESIDUAL 1
+#define WAMFFN_CROSS_RESIDUAL 2
+#define WAMFFN_FFN_RESIDUAL 3
+
+typedef struct wamffn_linear_plan wamffn_linear_plan;
+typedef struct wamffn_block_plan wamffn_block_plan;
+
+/* ABI version and the last error message of the calling thread. */
+int wamffn_abi_version(void);
+const char* wamffn_last_error(void);
+
+/* Number of kernels this library has launched in the process (all devices). */
+unsigned long long wamffn_launch_count(void);
+
+/* ------------------------------------------------------------------------
+ * Linear plan: y[rows, n_out] = act(x[rows, k_in] . weight[n_out, k_in]^T + bias)
+ * act = tanh-GELU when gelu != 0 (no bf16 rounding between bias and GELU,
+ * as in the reference's GELU_BIAS epilogue), identity otherwise.
+ * fp32 accumulation, bf16 output.  Replaces Plan(...) (cpp:161-174).
+ * `tune` != 0 times the candidate split-K factors on the device (like the
+ * reference's exhaustive candidate timing, cpp:121-158) and keeps the fastest;
+ * otherwise a static heuristic picks the configuration.
+ * ---------------------------------------------------------------------- */
+int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int gelu, int tune,
+                              wamffn_linear_plan** plan);
+int wamffn_linear_plan_destroy(wamffn_linear_plan* plan);
+
+/* Replaces Plan::run (cpp:177-188). out must hold rows*n_out bf16. */
+int wamffn_linear_run(wamffn_linear_plan* plan, void* stream, const void* x, const void* weight,
+                      const void* bias, void* out);
+
+/* Replaces Plan::selected_configuration (cpp:189).  Writes up to n values:
+ * {feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned}. */
+int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values, int n);
+
+/* Reads (and with clear != 0 resets) the device status word of a plan.
+ * Synchronises the device. */
+int wamffn_linear_status(wamffn_linear_plan* plan, uint32_t* status, int clear);
+
+/* PreparedFFN.forward (ffn.py:96-107): out = down(gelu(up(x))).  `up` and
+ * `down` are plans of matching rows; hidden is scratch owned by the up plan. */
+int wamffn_ffn_run(wamffn_linear_plan* up, wamffn_linear_plan* down, void* stream, const void* x,
+                   const void* w_up, const void* b_up, const void* w_down, const void* b_down,
+                   void* out);
+
+/* ------------------------------------------------------------------------
+ * Modulated norm (op wam_infer::modulated_norm, _triton_inference.py:130-221)
+ * x, update: [rows, dim] with row strides x_stride / update_stride (elements)
+ * mod, previous: [6, dim]; time: per-row [rows, 6, dim] with time_stride
+ * elements between rows, or time_stride == 0 for one shared [6, dim] row.
+ * weight, bias: [dim] (SELF_RESIDUAL only).  Outputs y, norm: [rows, dim]
+ * contiguous.  Batch 1, as the reference (grid = rows, _triton_inference.py:201).
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_norm_args {
+  const void* x;
+  int64_t x_stride;
+  const void* update;
+  int64_t update_stride;
+  const void* mod;
+  const void* previous;
+  const void* time;
+  int64_t time_stride;
+  const void* weight;
+  const void* bias;
+  void* y;
+  void* norm;
+  int rows;
+  int dim;
+  int mode;
+  float eps;
+} wamffn_norm_args;
+
+int wamffn_modulated_norm(void* stream, const wamffn_norm_args* args);
+
+/* ------------------------------------------------------------------------
+ * Fused FFN block (one DiT layer's FFN phase):
+ *   y      = bf16(x + update)                            (CROSS_RESIDUAL, update may be NULL)
+ *   n      = adaLN_{slots 3,4}(LayerNorm(y))             (_triton_inference.py:162-174)
+ *   a[j]   = n[indices[j]]                               (gather, blocks.py:249-251)
+ *   h      = bf16(gelu_tanh(a . W_up^T + b_up))          (up GEMM, tcgen05)
+ *   o[j]   = bf16(h . W_down^T + b_down)                 (down GEMM, tcgen05, split-K)
+ *   output[r] = o[j] where indices[j] == r; rows r < cache_rows that are not
+ *               gathered take cache_in[r]                (index_copy + cat, blocks.py:259-264)
+ *   cache_out[r] = output[r] for r < cache_rows          (token_outputs, blocks.py:264)
+ *   x_out  = bf16(y + bf16(gate . output)),
+ *            gate = bf16(mod[5] + time[r, 5])            (FFN_RESIDUAL fold / last layer,
+ *                                                         _triton_inference.py:158-161,
+ *                                                         blocks.py:265-268)
+ * With `normalized` set, the first two lines are skipped (y = x, n = normalized),
+ * matching VideoAdapter.ffn_at_layer_for_compile(layer_id, state, normalized, x)
+ * (blocks.py:246).
+ * indices: `rows` entries (int32 if index_bytes == 4, int64 if 8), -1 marks
+ * a pad row that is computed on zeros and never scattered; NULL means the
+ * identity (rows == seq).  Outputs that are NULL are not written.
+ * cache_in may equal cache_out (in-place history update).
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_block_args {
+  const void* x;          /* [seq, d] residual stream before the update */
+  const void* update;     /* [seq, d] cross-attention output or NULL */
+  const void* normalized; /* [seq, d] FFN input already normalised by the caller, or NULL.
+                             When set, the norm step is skipped: x is the residual y
+                             as-is (update must be NULL) and rows are gathered from here. */
+  const void* mod;        /* [6, d] block.modulation */
+  const void* time;       /* [seq, 6, d] per-token time modulation, or [6, d] */
+  int64_t time_stride;    /* elements between time rows; 0 = shared row */
+  const void* w_up;       /* [h, d] */
+  const void* b_up;       /* [h] */
+  const void* w_down;     /* [d, h] */
+  const void* b_down;     /* [d] */
+  const void* indices;    /* [rows] gather list or NULL */
+  int index_bytes;        /* 4 or 8 */
+  int rows;               /* gathered rows M */
+  int seq;                /* sequence rows S */
+  int cache_rows;         /* n: rows [0, n) are cacheable; 0 = no cache */
+  const void* cache_in;   /* [n, d] previous FFN outputs or NULL */
+  void* cache_out;        /* [n, d] or NULL */
+  void* y;                /* [seq, d] residual after the update, or NULL */
+  void* output;           /* [seq, d] FFN output in sequence order, or NULL */
+  void* x_out;            /* [seq, d] gated residual, or NULL */
+  float eps;              /* LayerNorm eps (norm2.eps) */
+} wamffn_block_args;
+
+/* Block plan: owns the gathered-activation, hidden and split-K scratch for up
+ * to max_rows gathered rows and max_seq sequence rows. */
+int wamffn_block_plan_create(int device, int max_rows, int max_seq, int d_model, int d_hidden,
+                             int tune, wamffn_block_plan** plan);
+int wamffn_block_plan_destroy(wamffn_block_plan* plan);
+int wamffn_block_run(wamffn_block_plan* plan, void* stream, const wamffn_block_args* args);
+int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear);
+/* {up: feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned,
+ *  down: same 7 values} for a given row count. */
+int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t* values, int n);
+
+/* ------------------------------------------------------------------------
+ * Token selection (select_tokens, approximation.py:55-67):
+ *   score[r] = 2 sum|now - before| / max(sum(|now| + |before|), 1e-6)  (fp32)
+ *   mandatory rows score +inf; the `count` best rows (stable descending, ties
+ *   to the smaller index) are written ascending to indices[0, count), then
+ *   indices[count + k] = n + k for k < seq - n.  features_out (optional)
+ *   receives a copy of the n current rows (the next request's history).
+ * now: [n, dim] rows `now_stride` elements apart; before: [n, dim];
+ * mandatory: n bytes (0/1) or NULL; indices: int64.  n <= 1024, count < n.
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_select_args {
+  const void* now;
+  int64_t now_stride;
+  const void* before;
+  const void* mandatory;
+  int n;
+  int dim;
+  int count;
+  int seq;
+  void* indices;
+  void* features_out;
+} wamffn_select_args;
+
+int wamffn_select_tokens(void* stream, const wamffn_select_args* args);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WAMFFN_H */

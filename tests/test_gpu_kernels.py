@@ -1,0 +1,196 @@
+"""GPU parity of the sm_100a kernels against the fp32 oracle.
+
+Tolerance: bf16 outputs within max-abs 2e-2 and
+mean-relative 5e-3 of the fp32 oracle; indices, cache positions and rows served
+from the cache are bit-exact.
+"""
+
+import pytest
+import torch
+
+from oracle import ffn as offn
+
+pytestmark = pytest.mark.gpu
+
+D, H = 3072, 14336
+MAX_ABS, MEAN_REL = 2e-2, 5e-3
+
+
+def close(actual, expected, max_abs=MAX_ABS, mean_rel=MEAN_REL):
+    a, e = actual.float(), expected.float()
+    err = (a - e).abs()
+    assert bool(torch.isfinite(a).all()), "non-finite output"
+    assert float(err.max()) <= max_abs, f"max abs {float(err.max()):.4g}"
+    rel = float(err.mean() / e.abs().mean().clamp_min(1e-12))
+    assert rel <= mean_rel, f"mean rel {rel:.4g}"
+
+
+@pytest.fixture(scope="module")
+def weights(cuda_device):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device=cuda_device).manual_seed(1234)
+
+    def rnd(*shape, std):
+        return (torch.randn(*shape, device=cuda_device, generator=g) * std).to(torch.bfloat16)
+
+    return dict(
+        w_up=rnd(H, D, std=0.02), b_up=rnd(H, std=0.01), w_down=rnd(D, H, std=0.02), b_down=rnd(D, std=0.01),
+        mod=rnd(1, 6, D, std=0.1), gen=g,
+    )
+
+
+def randn(shape, device, g, std=1.0):
+    return (torch.randn(*shape, device=device, generator=g) * std).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("rows", [1, 16, 17, 100, 240, 257, 272, 304, 336, 360, 392, 512])
+def test_up_projection_gelu(cuda_device, weights, rows):
+    from waminfer_b200.ffn import Plan
+
+    x = randn((rows, D), cuda_device, weights["gen"])
+    plan = Plan(x, weights["w_up"], weights["b_up"], exhaustive=False, gelu=True)
+    out = plan.run(x, weights["w_up"], weights["b_up"])
+    ref = offn.bf16(offn.gelu_tanh(x.float() @ weights["w_up"].float().T + weights["b_up"].float()))
+    close(out, ref)
+    assert plan.status() == 0
+    plan.close()
+
+
+@pytest.mark.parametrize("rows", [1, 17, 240, 272, 304, 360, 392, 512])
+def test_down_projection_split_k(cuda_device, weights, rows):
+    from waminfer_b200.ffn import Plan
+
+    h = randn((rows, H), cuda_device, weights["gen"], std=0.5)
+    plan = Plan(h, weights["w_down"], weights["b_down"], exhaustive=True, gelu=False)
+    out = plan.run(h, weights["w_down"], weights["b_down"])
+    ref = offn.bf16(h.float() @ weights["w_down"].float().T + weights["b_down"].float())
+    close(out, ref)
+    assert plan.selected_configuration()[-1] == 1  # tuned
+    assert plan.status() == 0
+    plan.close()
+
+
+def _block_inputs(cuda_device, weights, seq, per_token=True):
+    g = weights["gen"]
+    x = randn((1, seq, D), cuda_device, g)
+    update = randn((1, seq, D), cuda_device, g)
+    time = randn((1, seq, 6, D), cuda_device, g, std=0.1) if per_token else randn((1, 6, D), cuda_device, g, std=0.1)
+    return x, update, time
+
+
+def _oracle_block(x, update, normalized, mod, time, weights, indices, cache, n):
+    t = time[0].float()
+    return offn.ffn_block(
+        x[0].float(), None if update is None else update[0].float(),
+        None if normalized is None else normalized[0].float(), mod[0].float(), t,
+        weights["w_up"], weights["b_up"], weights["w_down"], weights["b_down"],
+        None if indices is None else indices.cpu(), None if cache is None else cache.reshape(-1, D).float(), n,
+        1e-6, ffn=lambda a, wu, bu, wd, bd: offn.prepared_ffn(a.to(wu.device), wu, bu, wd, bd).cpu())
+
+
+def _run_block(plan_id, x, update, normalized, mod, time, weights, indices, cache, n, want_output=True):
+    from waminfer_b200.blocks import ffn_block
+
+    return ffn_block(x, update, normalized, mod, time, weights["w_up"], weights["b_up"], weights["w_down"],
+                     weights["b_down"], indices, cache, n, plan_id, 1e-6, want_output)
+
+
+@pytest.fixture(scope="module")
+def block_plan(cuda_device):
+    from waminfer_b200.blocks import BlockPlan, register_block_plan, release_block_plan
+
+    plan_id = register_block_plan(BlockPlan(cuda_device, 512, 512, D, H))
+    yield plan_id
+    release_block_plan(plan_id)
+
+
+def _cpu(t):
+    return t.detach().float().cpu()
+
+
+@pytest.mark.parametrize("seq,per_token", [(392, True), (360, True), (240, False), (33, True)])
+def test_block_full_refresh(cuda_device, weights, block_plan, seq, per_token):
+    x, update, time = _block_inputs(cuda_device, weights, seq, per_token)
+    x_next, output, clean = _run_block(block_plan, x, update, None, weights["mod"], time, weights, None, None, 0)
+    rx, rout, _, _ = _oracle_block(_cpu(x), _cpu(update), None, _cpu(weights["mod"]), _cpu(time), weights, None,
+                                   None, 0)
+    close(output[0], rout)
+    close(x_next[0], rx)
+    assert clean.numel() == 0
+
+
+@pytest.mark.parametrize("count,index_dtype", [(32, torch.int64), (64, torch.int32), (96, torch.int64)])
+def test_block_token_reuse_reference_mode(cuda_device, weights, block_plan, count, index_dtype):
+    """Reference semantics: n = 120 current rows, `count` recomputed, 240 future
+    + 32 action rows always fresh; non-selected rows come from the cache."""
+    n, seq = 120, 392
+    g = torch.Generator().manual_seed(count)
+    chosen = torch.randperm(n, generator=g)[:count].sort().values
+    indices = torch.cat((chosen, torch.arange(n, seq))).to(index_dtype).to(cuda_device)
+    x, update, time = _block_inputs(cuda_device, weights, seq)
+    cache = randn((1, n, D), cuda_device, weights["gen"])
+    x_next, output, clean = _run_block(block_plan, x, update, None, weights["mod"], time, weights, indices, cache, n)
+    rx, rout, rclean, _ = _oracle_block(_cpu(x), _cpu(update), None, _cpu(weights["mod"]), _cpu(time), weights,
+                                        indices.long(), _cpu(cache), n)
+    kept = sorted(set(range(n)) - set(chosen.tolist()))
+    # Rows served from the cache are bit-exact copies, in the output and the new history.
+    assert torch.equal(output[0, kept].cpu(), cache[0, kept].cpu())
+    assert torch.equal(clean[0, kept].cpu(), cache[0, kept].cpu())
+    close(output[0], rout)
+    close(clean[0], rclean)
+    close(x_next[0], rx)
+
+
+def test_block_baseline_mode_with_pads(cuda_device, weights, block_plan):
+    """Per-frame selection over 3 latent frames (cache of 360 rows) with pad
+    entries (-1) that are computed on zeros and never scattered."""
+    n, seq, k, cap = 360, 392, 16, 32
+    g = torch.Generator().manual_seed(7)
+    entries = []
+    for f in range(3):
+        rows = (torch.randperm(120, generator=g)[:k].sort().values + 120 * f).tolist()
+        entries += rows + [-1] * (cap - k)
+    indices = torch.tensor(entries + list(range(n, seq)), dtype=torch.int32, device=cuda_device)
+    x, update, time = _block_inputs(cuda_device, weights, seq)
+    cache = randn((n, D), cuda_device, weights["gen"])
+    x_next, output, clean = _run_block(block_plan, x, update, None, weights["mod"], time, weights, indices, cache, n)
+    rx, rout, rclean, _ = _oracle_block(_cpu(x), _cpu(update), None, _cpu(weights["mod"]), _cpu(time), weights,
+                                        indices.long(), _cpu(cache), n)
+    selected = {r for r in entries if r >= 0}
+    kept = sorted(set(range(n)) - selected)
+    assert torch.equal(output[0, kept].cpu(), cache[kept].cpu())
+    close(output[0], rout)
+    close(clean[0], rclean)
+    close(x_next[0], rx)
+
+
+def test_block_pre_normalized_matches_fused(cuda_device, weights, block_plan):
+    """ffn_at_layer_for_compile's form (normalized given) equals the fused norm."""
+    from waminfer_b200.norm import CROSS_RESIDUAL, modulated_norm
+
+    seq, n, count = 392, 120, 32
+    indices = torch.cat((torch.arange(0, 120, 120 // count)[:count], torch.arange(n, seq))).to(cuda_device)
+    x, update, time = _block_inputs(cuda_device, weights, seq)
+    cache = randn((1, n, D), cuda_device, weights["gen"])
+    y, normalized = modulated_norm(x, update, weights["mod"], None, time, None, None, CROSS_RESIDUAL, 1e-6)
+    a = _run_block(block_plan, x, update, None, weights["mod"], time, weights, indices, cache, n)
+    b = _run_block(block_plan, y, None, normalized, weights["mod"], time, weights, indices, cache, n)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+
+
+def test_modulated_norm_matches_reference_kernel(cuda_device, golden):
+    from waminfer_b200.norm import modulated_norm
+
+    for c in golden("modulated_norm.pt"):
+        dev = lambda t: None if t is None else t.to(cuda_device)  # noqa: E731
+        mode = c["mode"]
+        y, n = modulated_norm(dev(c["x"]), dev(c["update"]) if mode else None, dev(c["mod"]),
+                              dev(c["previous"]) if mode == 3 else None, dev(c["time"]),
+                              dev(c["weight"]) if mode == 1 else None, dev(c["bias"]) if mode == 1 else None,
+                              mode, c["eps"])
+        assert torch.equal(y.cpu(), c["y"]), (c["dim"], mode)
+        diff = (n.cpu().float() - c["norm"].float()).abs()
+        ulp = c["norm"].float().abs().clamp_min(1e-3) * 2.0**-7
+        assert bool((diff <= ulp).all()), (c["dim"], mode)
+        assert float((diff > 0).float().mean()) < 0.01

@@ -1,0 +1,752 @@
+// C ABI of libwamffn: plans, tensor-map encoding, launch configuration.
+// See include/wamffn.h for the contract of every entry point.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gemm.cuh"
+#include "rowops.cuh"
+#include "select.cuh"
+#include "wamffn.h"
+
+using namespace wamffn;
+
+namespace {
+
+thread_local std::string g_error;
+std::atomic<unsigned long long> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+#define WAMFFN_CUDA(call)                                                                   \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess) return fail(WAMFFN_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && (prev == dev || cudaSetDevice(dev) == cudaSuccess))
+      ok = true;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool env_flag(const char* name, bool dflt) {
+  const char* v = getenv(name);
+  if (!v || !*v) return dflt;
+  return !(v[0] == '0' || v[0] == 'n' || v[0] == 'N' || v[0] == 'f' || v[0] == 'F');
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor [outer, inner] (inner contiguous, rows `row_bytes` apart),
+// box [box_outer, 64] with the 128-byte swizzle.
+int encode_operand(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return fail(WAMFFN_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {uint32_t(kBlockK), box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WAMFFN_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return WAMFFN_OK;
+}
+
+struct DeviceInfo {
+  int sm_count = 0;
+  bool ready = false;
+};
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+// Checks the device is an sm_100 part and raises the kernels' shared-memory limit once.
+int prepare_device(int device, int* sm_count) {
+  if (device < 0 || device >= 64) return fail(WAMFFN_ERR_INVALID, "bad device %d", device);
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceInfo& d = g_dev[device];
+  if (!d.ready) {
+    int major = 0, minor = 0;
+    WAMFFN_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    WAMFFN_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+    if (major != 10 || minor != 0)
+      return fail(WAMFFN_ERR_UNSUPPORTED, "libwamffn is built for sm_100a; device %d is sm_%d%d",
+                  device, major, minor);
+    WAMFFN_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device));
+    DeviceGuard g(device);
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemLimit));
+    d.ready = true;
+  }
+  *sm_count = d.sm_count;
+  return WAMFFN_OK;
+}
+
+// ---------------------------------------------------------------- GEMM config
+struct GemmConfig {
+  int rows = 0, n_out = 0, k_in = 0;
+  int tok_pad = 0, mma_n0 = 0, mma_n1 = 0, tok_box = 0, n_boxes = 0;
+  int stages = 0, splits = 1;
+  uint32_t tmem_cols = 0;
+  int smem_bytes = 0;
+};
+
+int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c) {
+  if (rows < 1 || rows > kMaxTokens)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d outside [1, %d]", rows, kMaxTokens);
+  if (n_out < kFeatTile || n_out % kFeatTile)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "n_out=%d must be a positive multiple of %d", n_out, kFeatTile);
+  if (k_in < kBlockK || k_in % kBlockK)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "k_in=%d must be a positive multiple of %d", k_in, kBlockK);
+  c->rows = rows;
+  c->n_out = n_out;
+  c->k_in = k_in;
+  c->tok_pad = (rows + 15) / 16 * 16;
+  if (c->tok_pad <= 256) {
+    c->mma_n0 = c->tok_pad;
+    c->mma_n1 = 0;
+    c->tok_box = c->tok_pad;
+    c->n_boxes = 1;
+  } else {
+    c->mma_n0 = (c->tok_pad / 16 + 1) / 2 * 16;
+    c->mma_n1 = c->tok_pad - c->mma_n0;
+    c->tok_box = c->tok_pad / 2;  // multiple of 8: each box starts on a 1024-byte swizzle atom
+    c->n_boxes = 2;
+  }
+  uint32_t cols = 32;
+  while (cols < uint32_t(c->tok_pad)) cols <<= 1;
+  c->tmem_cols = cols;
+  const int stage = gemm_a_bytes() + gemm_b_bytes(c->tok_pad);
+  c->stages = (kSmemLimit - kSmemReserve) / stage;
+  if (c->stages > kMaxStages) c->stages = kMaxStages;
+  if (c->stages < 2) return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d leaves fewer than 2 pipeline stages", rows);
+  const int k_blocks = k_in / kBlockK;
+  if (splits < 1) splits = 1;
+  if (splits > k_blocks) splits = k_blocks;
+  c->splits = splits;
+  c->smem_bytes = c->stages * stage + kSmemReserve;
+  return WAMFFN_OK;
+}
+
+// Split-K heuristic: fill the SMs with (feature tiles x splits) CTAs while
+// keeping at least 8 K blocks per split.
+int default_splits(int n_out, int k_in, int sm_count) {
+  const int tiles = n_out / kFeatTile;
+  const int k_blocks = k_in / kBlockK;
+  int best = 1;
+  for (int s = 1; s <= 16; ++s) {
+    if (tiles * s > sm_count) break;
+    if (k_blocks / s < 8) break;
+    best = s;
+  }
+  return best;
+}
+
+int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* weight, const void* act,
+                const void* bias, void* out, unsigned int* status, bool pdl) {
+  CUtensorMap tm_w, tm_x;
+  int rc = encode_operand(&tm_w, weight, uint64_t(c.k_in), uint64_t(c.n_out), uint64_t(c.k_in) * 2,
+                          kFeatTile);
+  if (rc) return rc;
+  rc = encode_operand(&tm_x, act, uint64_t(c.k_in), uint64_t(c.rows), uint64_t(c.k_in) * 2,
+                      uint32_t(c.tok_box));
+  if (rc) return rc;
+  GemmParams p{};
+  p.tokens = c.rows;
+  p.tok_pad = c.tok_pad;
+  p.mma_n0 = c.mma_n0;
+  p.mma_n1 = c.mma_n1;
+  p.tok_box = c.tok_box;
+  p.n_boxes = c.n_boxes;
+  p.k_blocks = c.k_in / kBlockK;
+  p.splits = c.splits;
+  p.stages = c.stages;
+  p.n_total = c.n_out;
+  p.tmem_cols = c.tmem_cols;
+  p.epi = epi;
+  p.pdl = 1;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.out = out;
+  p.status = status;
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(c.n_out / kFeatTile), unsigned(c.splits), 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = size_t(c.smem_bytes);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel, tm_w, tm_x, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
+int row_threads(int dim) {
+  int t = ((dim / 8) + 31) / 32 * 32;
+  if (t < 32) t = 32;
+  if (t > kRowThreads) t = kRowThreads;
+  return t;
+}
+
+int launch_norm(const NormParams& p, int grid, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(grid), 1, 1);
+  cfg.blockDim = dim3(unsigned(row_threads(p.dim)), 1, 1);
+  cfg.dynamicSmemBytes = size_t(p.dim) * sizeof(float);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, modnorm_kernel, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
+int launch_epi(const EpiParams& p, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(p.seq), 1, 1);
+  cfg.blockDim = dim3(unsigned(row_threads(p.dim)), 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, rowepi_kernel, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = env_flag("WAMFFN_PDL", true);
+  return on;
+}
+
+}  // namespace
+
+// ====================================================================== plans
+struct wamffn_linear_plan {
+  int device = 0;
+  int gelu = 0;
+  int tuned = 0;
+  GemmConfig cfg;
+  float* partial = nullptr;      // [splits, rows, n_out] when splits > 1
+  __nv_bfloat16* hidden = nullptr;  // [rows, n_out] scratch for wamffn_ffn_run (up plans)
+  unsigned int* status = nullptr;
+};
+
+struct wamffn_block_plan {
+  int device = 0;
+  int sm_count = 0;
+  int max_rows = 0, max_seq = 0, d = 0, h = 0;
+  int tune = 0;
+  __nv_bfloat16* gathered = nullptr;  // [max_rows, d]
+  __nv_bfloat16* hidden = nullptr;    // [max_rows, h]
+  __nv_bfloat16* y = nullptr;         // [max_seq, d] residual scratch when the caller wants no y
+  float* partial = nullptr;           // [max_splits, max_rows, d]
+  int max_splits = 1;
+  int* pos = nullptr;                 // [max_seq]
+  unsigned int* status = nullptr;
+  int split_override[kMaxTokens + 1];  // tuned split-K per row count (0 = heuristic)
+};
+
+namespace {
+
+int linear_execute(wamffn_linear_plan* plan, cudaStream_t stream, const void* x, const void* weight,
+                   const void* bias, void* out) {
+  const GemmConfig& c = plan->cfg;
+  const bool pdl = pdl_enabled();
+  if (c.splits == 1) {
+    return launch_gemm(c, plan->gelu ? EPI_GELU_BF16 : EPI_BIAS_BF16, stream, weight, x, bias, out,
+                       plan->status, pdl);
+  }
+  int rc = launch_gemm(c, EPI_PARTIAL_F32, stream, weight, x, nullptr, plan->partial, plan->status, pdl);
+  if (rc) return rc;
+  EpiParams e{};
+  e.partial = plan->partial;
+  e.splits = c.splits;
+  e.m = c.rows;
+  e.dim = c.n_out;
+  e.bias = static_cast<const __nv_bfloat16*>(bias);
+  e.pos_of_row = nullptr;
+  e.seq = c.rows;
+  e.output = static_cast<__nv_bfloat16*>(out);
+  e.status = plan->status;
+  e.pdl = 1;
+  return launch_epi(e, stream, pdl);
+}
+
+// Times `iters` launches of the plan on scratch operands; returns ms per launch.
+int time_linear(wamffn_linear_plan* plan, const void* x, const void* w, const void* b, void* out,
+                float* ms) {
+  cudaStream_t s;
+  WAMFFN_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  cudaEvent_t e0, e1;
+  WAMFFN_CUDA(cudaEventCreate(&e0));
+  WAMFFN_CUDA(cudaEventCreate(&e1));
+  int rc = WAMFFN_OK;
+  for (int i = 0; i < 3 && !rc; ++i) rc = linear_execute(plan, s, x, w, b, out);
+  const int iters = 16;
+  if (!rc) WAMFFN_CUDA(cudaEventRecord(e0, s));
+  for (int i = 0; i < iters && !rc; ++i) rc = linear_execute(plan, s, x, w, b, out);
+  if (!rc) {
+    WAMFFN_CUDA(cudaEventRecord(e1, s));
+    WAMFFN_CUDA(cudaEventSynchronize(e1));
+    float t = 0;
+    WAMFFN_CUDA(cudaEventElapsedTime(&t, e0, e1));
+    *ms = t / iters;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaStreamDestroy(s);
+  return rc;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wamffn_abi_version(void) { return WAMFFN_ABI_VERSION; }
+
+const char* wamffn_last_error(void) { return g_error.c_str(); }
+
+unsigned long long wamffn_launch_count(void) { return g_launches.load(); }
+
+int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int gelu, int tune,
+                              wamffn_linear_plan** out_plan) {
+  if (!out_plan) return fail(WAMFFN_ERR_INVALID, "plan output pointer is null");
+  *out_plan = nullptr;
+  GemmConfig probe;
+  int rc = make_gemm_config(rows, n_out, k_in, 1, &probe);
+  if (rc) return rc;
+  int sm = 0;
+  rc = prepare_device(device, &sm);
+  if (rc) return rc;
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", device);
+  {
+    // Creation allocates and may tune: refuse inside a capture, like the reference.
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    WAMFFN_CUDA(cudaStreamIsCapturing(cudaStreamLegacy, &st));
+    if (st != cudaStreamCaptureStatusNone)
+      return fail(WAMFFN_ERR_CAPTURE, "GEMM planning must finish before CUDA Graph capture");
+  }
+  auto* plan = new wamffn_linear_plan();
+  plan->device = device;
+  plan->gelu = gelu ? 1 : 0;
+  rc = make_gemm_config(rows, n_out, k_in, default_splits(n_out, k_in, sm), &plan->cfg);
+  if (rc) {
+    delete plan;
+    return rc;
+  }
+  auto cleanup = [&](int code) {
+    wamffn_linear_plan_destroy(plan);
+    return code;
+  };
+  if (cudaMalloc(&plan->status, sizeof(unsigned int)) != cudaSuccess ||
+      cudaMemset(plan->status, 0, sizeof(unsigned int)) != cudaSuccess)
+    return cleanup(fail(WAMFFN_ERR_CUDA, "status allocation failed"));
+  if (plan->gelu && cudaMalloc(&plan->hidden, size_t(rows) * n_out * 2) != cudaSuccess)
+    return cleanup(fail(WAMFFN_ERR_CUDA, "hidden scratch allocation failed"));
+  const int tiles = n_out / kFeatTile;
+  if (tune) {
+    // Candidate split-K factors are timed on scratch operands, the way the
+    // reference times every candidate algorithm (cpp:121-158).
+    int max_s = 1;
+    for (int s = 2; s <= 16 && tiles * s <= 2 * sm && (k_in / kBlockK) / s >= 4; ++s) max_s = s;
+    void *x = nullptr, *w = nullptr, *b = nullptr, *o = nullptr;
+    bool okalloc = cudaMalloc(&x, size_t(rows) * k_in * 2) == cudaSuccess &&
+                   cudaMalloc(&w, size_t(n_out) * k_in * 2) == cudaSuccess &&
+                   cudaMalloc(&b, size_t(n_out) * 2) == cudaSuccess &&
+                   cudaMalloc(&o, size_t(rows) * n_out * 2) == cudaSuccess &&
+                   (max_s == 1 || cudaMalloc(&plan->partial, size_t(max_s) * rows * n_out * 4) == cudaSuccess);
+    if (okalloc) {
+      cudaMemset(x, 0x3c, size_t(rows) * k_in * 2);
+      cudaMemset(w, 0x3c, size_t(n_out) * k_in * 2);
+      cudaMemset(b, 0, size_t(n_out) * 2);
+      float best = 1e30f;
+      int best_s = plan->cfg.splits;
+      for (int s = 1; s <= max_s; ++s) {
+        GemmConfig c;
+        if (make_gemm_config(rows, n_out, k_in, s, &c)) continue;
+        plan->cfg = c;
+        float ms = 0;
+        if (time_linear(plan, x, w, b, o, &ms) == WAMFFN_OK && ms < best) {
+          best = ms;
+          best_s = s;
+        }
+      }
+      make_gemm_config(rows, n_out, k_in, best_s, &plan->cfg);
+      plan->tuned = 1;
+    }
+    cudaFree(x);
+    cudaFree(w);
+    cudaFree(b);
+    cudaFree(o);
+    cudaFree(plan->partial);
+    plan->partial = nullptr;
+    cudaMemset(plan->status, 0, sizeof(unsigned int));
+    if (!okalloc) return cleanup(fail(WAMFFN_ERR_CUDA, "tuning scratch allocation failed"));
+  }
+  if (plan->cfg.splits > 1 &&
+      cudaMalloc(&plan->partial, size_t(plan->cfg.splits) * rows * n_out * sizeof(float)) != cudaSuccess)
+    return cleanup(fail(WAMFFN_ERR_CUDA, "split-K workspace allocation failed"));
+  *out_plan = plan;
+  return WAMFFN_OK;
+}
+
+int wamffn_linear_plan_destroy(wamffn_linear_plan* plan) {
+  if (!plan) return WAMFFN_OK;
+  DeviceGuard guard(plan->device);
+  cudaFree(plan->partial);
+  cudaFree(plan->hidden);
+  cudaFree(plan->status);
+  delete plan;
+  return WAMFFN_OK;
+}
+
+int wamffn_linear_run(wamffn_linear_plan* plan, void* stream, const void* x, const void* weight,
+                      const void* bias, void* out) {
+  if (!plan) return fail(WAMFFN_ERR_INVALID, "plan is null");
+  if (!x || !weight || !bias || !out) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(bias) || !aligned16(out))
+    return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
+  DeviceGuard guard(plan->device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", plan->device);
+  return linear_execute(plan, static_cast<cudaStream_t>(stream), x, weight, bias, out);
+}
+
+int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values, int n) {
+  if (!plan || !values) return fail(WAMFFN_ERR_INVALID, "null argument");
+  const GemmConfig& c = plan->cfg;
+  const uint32_t v[7] = {uint32_t(kFeatTile), uint32_t(c.tok_pad), uint32_t(c.mma_n1 > 0 ? 2 : 1),
+                         uint32_t(c.stages),   uint32_t(c.splits),  c.tmem_cols,
+                         uint32_t(plan->tuned)};
+  for (int i = 0; i < n && i < 7; ++i) values[i] = v[i];
+  return WAMFFN_OK;
+}
+
+int wamffn_linear_status(wamffn_linear_plan* plan, uint32_t* status, int clear) {
+  if (!plan || !status) return fail(WAMFFN_ERR_INVALID, "null argument");
+  DeviceGuard guard(plan->device);
+  WAMFFN_CUDA(cudaDeviceSynchronize());
+  WAMFFN_CUDA(cudaMemcpy(status, plan->status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  if (clear) WAMFFN_CUDA(cudaMemset(plan->status, 0, sizeof(uint32_t)));
+  return WAMFFN_OK;
+}
+
+int wamffn_ffn_run(wamffn_linear_plan* up, wamffn_linear_plan* down, void* stream, const void* x,
+                   const void* w_up, const void* b_up, const void* w_down, const void* b_down,
+                   void* out) {
+  if (!up || !down) return fail(WAMFFN_ERR_INVALID, "plan is null");
+  if (!up->gelu || !up->hidden) return fail(WAMFFN_ERR_INVALID, "the up plan must be a GELU plan");
+  if (up->cfg.rows != down->cfg.rows || up->cfg.n_out != down->cfg.k_in ||
+      up->cfg.k_in != down->cfg.n_out || up->device != down->device)
+    return fail(WAMFFN_ERR_INVALID, "up/down plans do not chain");
+  int rc = wamffn_linear_run(up, stream, x, w_up, b_up, up->hidden);
+  if (rc) return rc;
+  return wamffn_linear_run(down, stream, up->hidden, w_down, b_down, out);
+}
+
+int wamffn_modulated_norm(void* stream, const wamffn_norm_args* a) {
+  if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
+  if (a->rows < 1 || a->dim < 8 || a->dim % 8 || a->dim > 8 * 1024 * 4)
+    return fail(WAMFFN_ERR_INVALID, "rows=%d dim=%d unsupported (dim %% 8 == 0 required)", a->rows, a->dim);
+  if (a->mode < 0 || a->mode > 3) return fail(WAMFFN_ERR_INVALID, "mode %d", a->mode);
+  if (!a->x || !a->mod || !a->time || !a->y || !a->norm) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (a->mode > 0 && !a->update) return fail(WAMFFN_ERR_INVALID, "mode %d needs update", a->mode);
+  if (a->mode == WAMFFN_FFN_RESIDUAL && !a->previous) return fail(WAMFFN_ERR_INVALID, "mode 3 needs previous");
+  if (a->mode == WAMFFN_SELF_RESIDUAL && (!a->weight || !a->bias))
+    return fail(WAMFFN_ERR_INVALID, "mode 1 needs weight and bias");
+  const void* ptrs[] = {a->x, a->update, a->mod, a->previous, a->time, a->weight, a->bias, a->y, a->norm};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
+  if (a->x_stride % 8 || a->update_stride % 8 || a->time_stride % 8)
+    return fail(WAMFFN_ERR_INVALID, "row strides must be multiples of 8 elements");
+  int dev = 0;
+  WAMFFN_CUDA(cudaGetDevice(&dev));
+  NormParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(a->x);
+  p.xs = a->x_stride;
+  p.update = static_cast<const __nv_bfloat16*>(a->update);
+  p.us = a->update_stride;
+  p.mod = static_cast<const __nv_bfloat16*>(a->mod);
+  p.previous = static_cast<const __nv_bfloat16*>(a->previous);
+  p.time = static_cast<const __nv_bfloat16*>(a->time);
+  p.ts = a->time_stride;
+  p.weight = static_cast<const __nv_bfloat16*>(a->weight);
+  p.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  p.y = static_cast<__nv_bfloat16*>(a->y);
+  p.norm = static_cast<__nv_bfloat16*>(a->norm);
+  p.rows = a->rows;
+  p.dim = a->dim;
+  p.mode = a->mode;
+  p.eps = a->eps;
+  p.pdl = 1;
+  return launch_norm(p, a->rows, static_cast<cudaStream_t>(stream), pdl_enabled());
+}
+
+int wamffn_block_plan_create(int device, int max_rows, int max_seq, int d_model, int d_hidden,
+                             int tune, wamffn_block_plan** out_plan) {
+  if (!out_plan) return fail(WAMFFN_ERR_INVALID, "plan output pointer is null");
+  *out_plan = nullptr;
+  if (max_rows < 1 || max_rows > kMaxTokens || max_seq < 1)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "max_rows=%d max_seq=%d unsupported", max_rows, max_seq);
+  GemmConfig probe;
+  int rc = make_gemm_config(max_rows, d_hidden, d_model, 1, &probe);
+  if (rc) return rc;
+  rc = make_gemm_config(max_rows, d_model, d_hidden, 1, &probe);
+  if (rc) return rc;
+  int sm = 0;
+  rc = prepare_device(device, &sm);
+  if (rc) return rc;
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", device);
+  auto* plan = new wamffn_block_plan();
+  plan->device = device;
+  plan->sm_count = sm;
+  plan->max_rows = max_rows;
+  plan->max_seq = max_seq;
+  plan->d = d_model;
+  plan->h = d_hidden;
+  plan->tune = tune;
+  memset(plan->split_override, 0, sizeof(plan->split_override));
+  plan->max_splits = 16;
+  auto cleanup = [&](int code) {
+    wamffn_block_plan_destroy(plan);
+    return code;
+  };
+  bool ok = cudaMalloc(&plan->gathered, size_t(max_rows) * d_model * 2) == cudaSuccess &&
+            cudaMalloc(&plan->hidden, size_t(max_rows) * d_hidden * 2) == cudaSuccess &&
+            cudaMalloc(&plan->y, size_t(max_seq) * d_model * 2) == cudaSuccess &&
+            cudaMalloc(&plan->partial, size_t(plan->max_splits) * max_rows * d_model * 4) == cudaSuccess &&
+            cudaMalloc(&plan->pos, size_t(max_seq) * sizeof(int)) == cudaSuccess &&
+            cudaMalloc(&plan->status, sizeof(unsigned int)) == cudaSuccess &&
+            cudaMemset(plan->status, 0, sizeof(unsigned int)) == cudaSuccess;
+  if (!ok) return cleanup(fail(WAMFFN_ERR_CUDA, "block plan allocation failed"));
+  *out_plan = plan;
+  return WAMFFN_OK;
+}
+
+int wamffn_block_plan_destroy(wamffn_block_plan* plan) {
+  if (!plan) return WAMFFN_OK;
+  DeviceGuard guard(plan->device);
+  cudaFree(plan->gathered);
+  cudaFree(plan->hidden);
+  cudaFree(plan->y);
+  cudaFree(plan->partial);
+  cudaFree(plan->pos);
+  cudaFree(plan->status);
+  delete plan;
+  return WAMFFN_OK;
+}
+
+namespace {
+int block_configs(const wamffn_block_plan* plan, int rows, GemmConfig* up, GemmConfig* down) {
+  int rc = make_gemm_config(rows, plan->h, plan->d, default_splits(plan->h, plan->d, plan->sm_count), up);
+  if (rc) return rc;
+  int s = plan->split_override[rows];
+  if (s <= 0) s = default_splits(plan->d, plan->h, plan->sm_count);
+  if (s > plan->max_splits) s = plan->max_splits;
+  return make_gemm_config(rows, plan->d, plan->h, s, down);
+}
+}  // namespace
+
+int wamffn_block_run(wamffn_block_plan* plan, void* stream_, const wamffn_block_args* a) {
+  if (!plan || !a) return fail(WAMFFN_ERR_INVALID, "null argument");
+  if (a->rows < 1 || a->rows > plan->max_rows)
+    return fail(WAMFFN_ERR_INVALID, "rows=%d outside [1, %d]", a->rows, plan->max_rows);
+  if (a->seq < 1 || a->seq > plan->max_seq)
+    return fail(WAMFFN_ERR_INVALID, "seq=%d outside [1, %d]", a->seq, plan->max_seq);
+  if (!a->indices && a->rows != a->seq)
+    return fail(WAMFFN_ERR_INVALID, "without indices rows (%d) must equal seq (%d)", a->rows, a->seq);
+  if (a->indices && a->index_bytes != 4 && a->index_bytes != 8)
+    return fail(WAMFFN_ERR_INVALID, "index_bytes must be 4 or 8");
+  if (a->cache_rows < 0 || a->cache_rows > a->seq)
+    return fail(WAMFFN_ERR_INVALID, "cache_rows=%d outside [0, seq]", a->cache_rows);
+  if (a->cache_rows > 0 && a->indices && !a->cache_in)
+    return fail(WAMFFN_ERR_INVALID, "a gathered block with cache rows needs cache_in");
+  if (!a->x || !a->mod || !a->time || !a->w_up || !a->b_up || !a->w_down || !a->b_down)
+    return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (a->normalized && a->update)
+    return fail(WAMFFN_ERR_INVALID, "a pre-normalised input takes no update (it is already folded in)");
+  if (a->time_stride % 8) return fail(WAMFFN_ERR_INVALID, "time_stride must be a multiple of 8");
+  const void* ptrs[] = {a->x, a->update, a->normalized, a->mod, a->time, a->w_up, a->b_up, a->w_down,
+                        a->b_down, a->cache_in, a->cache_out, a->y, a->output, a->x_out};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
+  DeviceGuard guard(plan->device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", plan->device);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const bool pdl = pdl_enabled();
+  GemmConfig up, down;
+  int rc = block_configs(plan, a->rows, &up, &down);
+  if (rc) return rc;
+
+  // With a pre-normalised input the residual is the caller's x itself.
+  const __nv_bfloat16* y =
+      a->normalized ? static_cast<const __nv_bfloat16*>(a->x)
+                    : static_cast<const __nv_bfloat16*>(a->y ? a->y : plan->y);
+  // 1. CROSS_RESIDUAL norm (or plain copy) + gather into the activation operand.
+  NormParams n{};
+  n.gather_only = a->normalized ? 1 : 0;
+  n.x = static_cast<const __nv_bfloat16*>(a->normalized ? a->normalized : a->x);
+  n.xs = plan->d;
+  n.update = static_cast<const __nv_bfloat16*>(a->update);
+  n.us = plan->d;
+  n.mod = static_cast<const __nv_bfloat16*>(a->mod);
+  n.time = static_cast<const __nv_bfloat16*>(a->time);
+  n.ts = a->time_stride;
+  n.y = a->normalized ? nullptr : const_cast<__nv_bfloat16*>(y);
+  n.norm = nullptr;
+  n.rows = a->seq;
+  n.dim = plan->d;
+  n.mode = WAMFFN_CROSS_RESIDUAL;
+  n.eps = a->eps;
+  n.idx = a->indices;
+  n.idx_bytes = a->index_bytes;
+  n.m = a->rows;
+  n.gathered = plan->gathered;
+  n.pos_of_row = plan->pos;
+  n.status = plan->status;
+  n.pdl = 1;
+  rc = launch_norm(n, a->seq > a->rows ? a->seq : a->rows, stream, pdl);
+  if (rc) return rc;
+  // 2. up projection + bias + GELU -> hidden.
+  rc = launch_gemm(up, EPI_GELU_BF16, stream, a->w_up, plan->gathered, a->b_up, plan->hidden,
+                   plan->status, pdl);
+  if (rc) return rc;
+  // 3. down projection, split-K fp32 partials.
+  rc = launch_gemm(down, EPI_PARTIAL_F32, stream, a->w_down, plan->hidden, nullptr, plan->partial,
+                   plan->status, pdl);
+  if (rc) return rc;
+  // 4. reduce + bias, scatter into the cache, gated residual.
+  EpiParams e{};
+  e.partial = plan->partial;
+  e.splits = down.splits;
+  e.m = a->rows;
+  e.dim = plan->d;
+  e.bias = static_cast<const __nv_bfloat16*>(a->b_down);
+  e.pos_of_row = plan->pos;
+  e.seq = a->seq;
+  e.cache_rows = a->cache_rows;
+  e.cache_in = static_cast<const __nv_bfloat16*>(a->cache_in);
+  e.cache_out = static_cast<__nv_bfloat16*>(a->cache_out);
+  e.output = static_cast<__nv_bfloat16*>(a->output);
+  e.y = y;
+  e.mod = static_cast<const __nv_bfloat16*>(a->mod);
+  e.time = static_cast<const __nv_bfloat16*>(a->time);
+  e.ts = a->time_stride;
+  e.x_out = static_cast<__nv_bfloat16*>(a->x_out);
+  e.status = plan->status;
+  e.pdl = 1;
+  return launch_epi(e, stream, pdl);
+}
+
+int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear) {
+  if (!plan || !status) return fail(WAMFFN_ERR_INVALID, "null argument");
+  DeviceGuard guard(plan->device);
+  WAMFFN_CUDA(cudaDeviceSynchronize());
+  WAMFFN_CUDA(cudaMemcpy(status, plan->status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
+  if (clear) WAMFFN_CUDA(cudaMemset(plan->status, 0, sizeof(uint32_t)));
+  return WAMFFN_OK;
+}
+
+int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t* values, int n) {
+  if (!plan || !values) return fail(WAMFFN_ERR_INVALID, "null argument");
+  GemmConfig up, down;
+  int rc = block_configs(plan, rows, &up, &down);
+  if (rc) return rc;
+  const GemmConfig* cs[2] = {&up, &down};
+  int k = 0;
+  for (const GemmConfig* c : cs) {
+    const uint32_t v[7] = {uint32_t(kFeatTile), uint32_t(c->tok_pad), uint32_t(c->mma_n1 > 0 ? 2 : 1),
+                           uint32_t(c->stages),  uint32_t(c->splits),  c->tmem_cols, 0u};
+    for (int i = 0; i < 7 && k < n; ++i) values[k++] = v[i];
+  }
+  return WAMFFN_OK;
+}
+
+int wamffn_select_tokens(void* stream, const wamffn_select_args* a) {
+  if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
+  if (a->n < 1 || a->n > kSelectThreads) return fail(WAMFFN_ERR_UNSUPPORTED, "n=%d outside [1, %d]", a->n, kSelectThreads);
+  if (a->count < 1 || a->count >= a->n) return fail(WAMFFN_ERR_INVALID, "count=%d must be in [1, n)", a->count);
+  if (a->seq < a->n) return fail(WAMFFN_ERR_INVALID, "seq=%d < n=%d", a->seq, a->n);
+  if (a->dim < 8 || a->dim % 8) return fail(WAMFFN_ERR_INVALID, "dim=%d must be a multiple of 8", a->dim);
+  if (!a->now || !a->before || !a->indices) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(a->now) || !aligned16(a->before) || (a->features_out && !aligned16(a->features_out)) ||
+      a->now_stride % 8)
+    return fail(WAMFFN_ERR_INVALID, "rows must be 16-byte aligned");
+  SelectParams p{};
+  p.now = static_cast<const __nv_bfloat16*>(a->now);
+  p.now_stride = a->now_stride;
+  p.before = static_cast<const __nv_bfloat16*>(a->before);
+  p.mandatory = static_cast<const unsigned char*>(a->mandatory);
+  p.n = a->n;
+  p.dim = a->dim;
+  p.count = a->count;
+  p.seq = a->seq;
+  p.indices = static_cast<long long*>(a->indices);
+  p.features_out = static_cast<__nv_bfloat16*>(a->features_out);
+  p.pdl = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(kSelectThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, select_tokens_kernel, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
+}  // extern "C"

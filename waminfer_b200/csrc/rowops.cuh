@@ -1,0 +1,303 @@
+// Row kernels around the two FFN GEMMs.  Both are HBM/L2-bound elementwise
+// passes: one CTA per sequence row, 16-byte vector loads/stores.
+//
+// modnorm_kernel  -- the reference's modulated norm (all four MODEs of
+//                    WAMInfer/_triton_inference.py:130-176) with an optional
+//                    fused row gather into the GEMM activation buffer
+//                    (blocks.py:249-251).
+// rowepi_kernel   -- split-K reduction + bias of the down projection, the
+//                    cache scatter/concat (blocks.py:259-264) and the gated
+//                    residual (_triton_inference.py:158-161, blocks.py:265-268).
+#pragma once
+
+#include "ptx.cuh"
+#include "wamffn.h"
+
+namespace wamffn {
+
+constexpr int kRowThreads = 384;   // 3072 / 8: one 16-byte vector per thread at d = 3072
+constexpr int kMaxMatches = 32;    // gather entries naming one row (duplicates) tracked per CTA
+
+struct NormParams {
+  const __nv_bfloat16* x;
+  long long xs;
+  const __nv_bfloat16* update;
+  long long us;
+  const __nv_bfloat16* mod;
+  const __nv_bfloat16* previous;
+  const __nv_bfloat16* time;
+  long long ts;
+  const __nv_bfloat16* weight;
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* y;      // [rows, dim] or null
+  __nv_bfloat16* norm;   // [rows, dim] or null
+  int rows;
+  int dim;
+  int mode;
+  float eps;
+  const void* idx;       // gather list or null (identity when gathered != null)
+  int idx_bytes;
+  int m;                 // gathered rows
+  __nv_bfloat16* gathered;  // [m, dim] or null
+  int* pos_of_row;       // [rows] or null: last j with idx[j] == row, -1 if none
+  unsigned int* status;
+  int pdl;
+  int gather_only;       // 1: x is already normalised; only gather rows (no y / norm)
+};
+
+struct EpiParams {
+  const float* partial;  // [splits, m, dim]
+  int splits;
+  int m;
+  int dim;
+  const __nv_bfloat16* bias;
+  const int* pos_of_row;  // [seq] or null (identity)
+  int seq;
+  int cache_rows;
+  const __nv_bfloat16* cache_in;
+  __nv_bfloat16* cache_out;
+  __nv_bfloat16* output;
+  const __nv_bfloat16* y;
+  const __nv_bfloat16* mod;
+  const __nv_bfloat16* time;
+  long long ts;
+  __nv_bfloat16* x_out;
+  unsigned int* status;
+  int pdl;
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// bf16(mod[slot] + time[row, slot]) for 8 consecutive features (the
+// reference's _modulation helper, _triton_inference.py:123-127).
+__device__ __forceinline__ void modulation8(const __nv_bfloat16* mod, const __nv_bfloat16* time,
+                                            long long ts, int row, int slot, int dim, int e,
+                                            float (&out)[8]) {
+  float a[8], b[8];
+  load8(mod + size_t(slot) * dim + e, a);
+  load8(time + size_t(row) * ts + size_t(slot) * dim + e, b);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = bf16_round(a[i] + b[i]);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  __syncthreads();  // red[] may still be read by a previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < nwarps; ++w) s += red[w];  // fixed order: deterministic
+  return s;
+}
+
+__device__ __forceinline__ long long load_index(const void* idx, int bytes, int j) {
+  return bytes == 8 ? reinterpret_cast<const long long*>(idx)[j]
+                    : static_cast<long long>(reinterpret_cast<const int*>(idx)[j]);
+}
+
+// Dynamic shared memory: dim floats (the row after the residual update).
+__global__ void __launch_bounds__(kRowThreads) modnorm_kernel(const NormParams p) {
+  extern __shared__ float xrow[];
+  __shared__ float red[32];
+  __shared__ int matches[kMaxMatches];
+  __shared__ int n_match;
+  __shared__ int last_match;
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nvec = p.dim >> 3;
+
+  if (p.pdl) pdl_wait_prior();
+
+  // Pad / invalid gather entries: the activation row is zero so the GEMM
+  // computes on defined data; invalid ones also raise the status bit.
+  if (p.gathered != nullptr && p.idx != nullptr && b < p.m) {
+    const long long r = load_index(p.idx, p.idx_bytes, b);
+    if (r < 0 || r >= p.rows) {
+      if (r != -1 && tid == 0) atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+      for (int v = tid; v < nvec; v += blockDim.x)
+        *reinterpret_cast<uint4*>(p.gathered + size_t(b) * p.dim + v * 8) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (b >= p.rows) return;
+  const int row = b;
+
+  // Which gathered slots read this row?
+  if (tid == 0) {
+    n_match = 0;
+    last_match = -1;
+  }
+  __syncthreads();
+  if (p.gathered != nullptr) {
+    if (p.idx == nullptr) {
+      if (tid == 0 && row < p.m) {
+        matches[0] = row;
+        n_match = 1;
+        last_match = row;
+      }
+    } else {
+      for (int j = tid; j < p.m; j += blockDim.x) {
+        if (load_index(p.idx, p.idx_bytes, j) == row) {
+          const int slot = atomicAdd(&n_match, 1);
+          if (slot < kMaxMatches) matches[slot] = j;
+          else atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+          atomicMax(&last_match, j);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (p.pos_of_row != nullptr && tid == 0) p.pos_of_row[row] = last_match;
+
+  if (p.gather_only) {
+    const int nm = n_match < kMaxMatches ? n_match : kMaxMatches;
+    const __nv_bfloat16* src = p.x + size_t(row) * p.xs;
+    for (int v = tid; v < nvec; v += blockDim.x) {
+      const uint4 val = *reinterpret_cast<const uint4*>(src + v * 8);
+      for (int k = 0; k < nm; ++k)
+        *reinterpret_cast<uint4*>(p.gathered + size_t(matches[k]) * p.dim + v * 8) = val;
+    }
+    if (tid == 0) pdl_launch_dependents();
+    return;
+  }
+
+  // Pass 1: residual update (bf16 rounding after each step) and the row sum.
+  const __nv_bfloat16* xr = p.x + size_t(row) * p.xs;
+  float local = 0.f;
+  for (int v = tid; v < nvec; v += blockDim.x) {
+    const int e = v * 8;
+    float x[8];
+    load8(xr + e, x);
+    if (p.mode > 0 && p.update != nullptr) {
+      float u[8];
+      load8(p.update + size_t(row) * p.us + e, u);
+      if (p.mode == WAMFFN_SELF_RESIDUAL || p.mode == WAMFFN_FFN_RESIDUAL) {
+        float g[8];
+        if (p.mode == WAMFFN_SELF_RESIDUAL) modulation8(p.mod, p.time, p.ts, row, 2, p.dim, e, g);
+        else modulation8(p.previous, p.time, p.ts, row, 5, p.dim, e, g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i] = bf16_round(g[i] * u[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = bf16_round(x[i] + u[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xrow[e + i] = x[i];
+      local += x[i];
+    }
+    if (p.y != nullptr) store8(p.y + size_t(row) * p.dim + e, x);
+  }
+  const float mean = block_sum(local, red) / float(p.dim);
+
+  // Pass 2: centred second moment.
+  local = 0.f;
+  for (int v = tid; v < nvec; v += blockDim.x) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float c = xrow[v * 8 + i] - mean;
+      local += c * c;
+    }
+  }
+  const float var = block_sum(local, red) / float(p.dim);
+  const float rstd = rsqrtf(var + p.eps);
+
+  // Pass 3: normalise, modulate, write norm and the gathered copies.
+  const int sh = p.mode == WAMFFN_CROSS_RESIDUAL ? 3 : 0;
+  const int sc = p.mode == WAMFFN_CROSS_RESIDUAL ? 4 : 1;
+  const int nm = n_match < kMaxMatches ? n_match : kMaxMatches;
+  for (int v = tid; v < nvec; v += blockDim.x) {
+    const int e = v * 8;
+    float n[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = (xrow[e + i] - mean) * rstd;
+    if (p.mode == WAMFFN_SELF_RESIDUAL) {
+      float w[8], bb[8];
+      load8(p.weight + e, w);
+      load8(p.bias + e, bb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) n[i] = n[i] * w[i] + bb[i];
+    } else {
+      float shift[8], scale[8];
+      modulation8(p.mod, p.time, p.ts, row, sh, p.dim, e, shift);
+      modulation8(p.mod, p.time, p.ts, row, sc, p.dim, e, scale);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float s1 = bf16_round(1.0f + scale[i]);
+        n[i] = bf16_round(bf16_round(n[i]) * s1) + shift[i];
+      }
+    }
+    if (p.norm != nullptr) store8(p.norm + size_t(row) * p.dim + e, n);
+    for (int k = 0; k < nm; ++k) store8(p.gathered + size_t(matches[k]) * p.dim + e, n);
+  }
+  if (tid == 0) pdl_launch_dependents();
+}
+
+// One CTA per sequence row.
+__global__ void __launch_bounds__(kRowThreads) rowepi_kernel(const EpiParams p) {
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nvec = p.dim >> 3;
+  if (p.pdl) pdl_wait_prior();
+  int j = p.pos_of_row != nullptr ? p.pos_of_row[row] : row;
+  if (j >= p.m) j = -1;
+  const bool cached_row = row < p.cache_rows;
+  if (j < 0 && !cached_row && tid == 0 && p.status) atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+  for (int v = tid; v < nvec; v += blockDim.x) {
+    const int e = v * 8;
+    float o[8];
+    if (j >= 0) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int s = 0; s < p.splits; ++s) {
+        const float4* src =
+            reinterpret_cast<const float4*>(p.partial + (size_t(s) * p.m + j) * p.dim + e);
+        const float4 a = src[0], c = src[1];
+        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        acc[4] += c.x; acc[5] += c.y; acc[6] += c.z; acc[7] += c.w;
+      }
+      float bb[8];
+      load8(p.bias + e, bb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = bf16_round(acc[i] + bb[i]);
+    } else if (cached_row && p.cache_in != nullptr) {
+      load8(p.cache_in + size_t(row) * p.dim + e, o);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    }
+    if (p.output != nullptr) store8(p.output + size_t(row) * p.dim + e, o);
+    if (cached_row && p.cache_out != nullptr) store8(p.cache_out + size_t(row) * p.dim + e, o);
+    if (p.x_out != nullptr) {
+      float g[8], y[8], r[8];
+      modulation8(p.mod, p.time, p.ts, row, 5, p.dim, e, g);
+      load8(p.y + size_t(row) * p.dim + e, y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) r[i] = y[i] + bf16_round(g[i] * o[i]);
+      store8(p.x_out + size_t(row) * p.dim + e, r);
+    }
+  }
+  if (tid == 0) pdl_launch_dependents();
+}
+
+}  // namespace wamffn

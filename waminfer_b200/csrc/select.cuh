@@ -1,0 +1,89 @@
+// Token selection for cross-observation FFN reuse (WAMInfer/approximation.py:55-67).
+//
+// score[r] = 2 * sum_k |now[r,k] - before[r,k]| / max(sum_k |now[r,k]| + |before[r,k]|, 1e-6)
+// in fp32; mandatory rows score +inf.  The `count` best rows by descending
+// score (ties: smaller index first, i.e. a stable descending sort) are written
+// in ascending order, followed by the future rows n..seq-1.
+//
+// One CTA: n <= 1024 rows of the current frame.  Ranking is an all-pairs count
+// (n^2 comparisons), which is exact and order-independent.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace wamffn {
+
+constexpr int kSelectThreads = 1024;
+
+struct SelectParams {
+  const __nv_bfloat16* now;     // [n, dim] rows with stride now_stride
+  long long now_stride;
+  const __nv_bfloat16* before;  // [n, dim] contiguous
+  const unsigned char* mandatory;  // [n] (bool) or null
+  int n;
+  int dim;
+  int count;
+  int seq;
+  long long* indices;           // [count + seq - n]
+  __nv_bfloat16* features_out;  // [n, dim] copy of `now` or null
+  int pdl;
+};
+
+__global__ void __launch_bounds__(kSelectThreads) select_tokens_kernel(const SelectParams p) {
+  __shared__ float score[kSelectThreads];
+  __shared__ int chosen[kSelectThreads];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nwarps = blockDim.x >> 5;
+  if (p.pdl) pdl_wait_prior();
+
+  for (int r = warp; r < p.n; r += nwarps) {
+    const __nv_bfloat16* a = p.now + size_t(r) * p.now_stride;
+    const __nv_bfloat16* b = p.before + size_t(r) * p.dim;
+    float num = 0.f, den = 0.f;
+    for (int e = lane * 8; e < p.dim; e += 32 * 8) {
+      const uint4 ua = *reinterpret_cast<const uint4*>(a + e);
+      const uint4 ub = *reinterpret_cast<const uint4*>(b + e);
+      if (p.features_out) *reinterpret_cast<uint4*>(p.features_out + size_t(r) * p.dim + e) = ua;
+      const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&ua);
+      const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&ub);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 fa = __bfloat1622float2(ha[i]);
+        const float2 fb = __bfloat1622float2(hb[i]);
+        num += fabsf(fa.x - fb.x) + fabsf(fa.y - fb.y);
+        den += (fabsf(fa.x) + fabsf(fb.x)) + (fabsf(fa.y) + fabsf(fb.y));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      num += __shfl_xor_sync(0xffffffffu, num, o);
+      den += __shfl_xor_sync(0xffffffffu, den, o);
+    }
+    if (lane == 0) {
+      float s = (2.0f * num) / fmaxf(den, 1e-6f);
+      if (p.mandatory && p.mandatory[r]) s = __int_as_float(0x7f800000);  // +inf
+      score[r] = s;
+    }
+  }
+  __syncthreads();
+  if (tid < p.n) {
+    const float s = score[tid];
+    int rank = 0;
+    for (int j = 0; j < p.n; ++j) {
+      const float t = score[j];
+      rank += (t > s) || (t == s && j < tid);
+    }
+    chosen[tid] = rank < p.count;
+  }
+  __syncthreads();
+  if (tid < p.n && chosen[tid]) {
+    int pos = 0;
+    for (int j = 0; j < tid; ++j) pos += chosen[j];
+    p.indices[pos] = tid;
+  }
+  for (int k = tid; k < p.seq - p.n; k += blockDim.x) p.indices[p.count + k] = p.n + k;
+  if (tid == 0) pdl_launch_dependents();
+}
+
+}  // namespace wamffn

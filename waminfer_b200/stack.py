@@ -1,0 +1,166 @@
+"""30-layer video-DiT FFN stack on the fused block kernels.
+
+A *request* here is the FFN work of one WAMInfer observation under the 2F
+motion-adaptive schedule with cross-observation token reuse
+(``WAMInfer/runtime.py:157-201``, ``WAMInfer/approximation.py:70-84``): the
+Transformer runs at Euler updates 0 and 3 only, so the FFN stack runs twice.
+
+* update 0 (token reuse): layer 0 recomputes every row
+  (``WAMInfer/blocks.py:248``); layers 1..L-1 gather the ``count`` selected
+  current-frame rows plus every future-frame and action row, and scatter the
+  recomputed current rows into the per-layer history ``[L-1, n, d]``
+  (``WAMInfer/blocks.py:249-264``, ``WAMInfer/runtime.py:263``).
+* update 3 (full refresh): every row of every layer.
+
+Each layer is one ``wamffn_block_run`` (norm + gather, up GEMM, down GEMM,
+reduce + scatter + gated residual); layers chain through ping-pong residual
+buffers.  Everything a request touches is preallocated, so a request (or a
+batch of them) can be captured into one CUDA graph.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from waminfer_b200 import _lib
+from waminfer_b200.blocks import BlockPlan
+
+
+@dataclass
+class LayerWeights:
+    w_up: torch.Tensor    # [h, d]
+    b_up: torch.Tensor    # [h]
+    w_down: torch.Tensor  # [d, h]
+    b_down: torch.Tensor  # [d]
+    mod: torch.Tensor     # [1, 6, d] block.modulation
+
+
+def make_weights(layers: int, d: int, h: int, device, seed: int = 0) -> list[LayerWeights]:
+    """Seeded synthetic weights: W ~ N(0, 0.02), biases ~ N(0, 0.01), modulation ~ N(0, 0.1)."""
+    out = []
+    for layer in range(layers):
+        g = torch.Generator(device=device).manual_seed(seed * 1000 + layer)
+
+        def rnd(*shape, std):
+            return (torch.randn(*shape, device=device, generator=g) * std).to(torch.bfloat16)
+
+        out.append(LayerWeights(rnd(h, d, std=0.02), rnd(h, std=0.01), rnd(d, h, std=0.02), rnd(d, std=0.01),
+                                rnd(1, 6, d, std=0.1)))
+    return out
+
+
+def ffn_flops(rows: int, d: int, h: int) -> int:
+    """Algorithmic FLOPs of one FFN layer over `rows` real rows: 2 GEMMs of 2*M*d*h."""
+    return 4 * rows * d * h
+
+
+@dataclass
+class Geometry:
+    """Row counts of one request (default: 384x320 RGB, 9 frames -> 3 latent
+    frames of 12x10 tokens, 32 action rows carried with the video rows)."""
+
+    layers: int = 30
+    d: int = 3072
+    h: int = 14336
+    current: int = 120     # n: current-observation rows (cacheable)
+    future: int = 240      # future-frame rows (always recomputed)
+    action: int = 32       # action rows (always recomputed)
+    count: int = 32        # refreshed current rows (capacity bucket)
+
+    @property
+    def seq(self) -> int:
+        return self.current + self.future + self.action
+
+    @property
+    def reuse_rows(self) -> int:
+        return self.count + self.future + self.action
+
+    def request_rows(self) -> list[int]:
+        """Rows of each of the 2*L layer passes of one 2F request."""
+        return [self.seq] + [self.reuse_rows] * (self.layers - 1) + [self.seq] * self.layers
+
+    def request_flops(self) -> int:
+        return sum(ffn_flops(m, self.d, self.h) for m in self.request_rows())
+
+
+class Request:
+    """Device buffers of one request: inputs of both passes, the history it
+    reads and the history it writes."""
+
+    def __init__(self, geo: Geometry, device, seed: int, history_in: torch.Tensor | None = None):
+        g = torch.Generator(device=device).manual_seed(10_000 + seed)
+        s, d = geo.seq, geo.d
+
+        def rnd(*shape, std=1.0):
+            return (torch.randn(*shape, device=device, generator=g) * std).to(torch.bfloat16)
+
+        self.x = [rnd(s, d), rnd(s, d)]                    # residual stream entering update 0 / update 3
+        self.time = [rnd(s, 6, d, std=0.1), rnd(s, 6, d, std=0.1)]  # per-token time modulation per update
+        cg = torch.Generator().manual_seed(20_000 + seed)
+        chosen = torch.randperm(geo.current, generator=cg)[: geo.count].sort().values
+        self.indices = torch.cat((chosen, torch.arange(geo.current, s))).to(torch.int64).to(device)
+        self.history_in = history_in if history_in is not None else rnd(geo.layers - 1, geo.current, d)
+        self.history_out = torch.empty_like(self.history_in)
+        self.out = [torch.empty(s, d, device=device, dtype=torch.bfloat16) for _ in range(2)]
+
+
+class FFNStack:
+    """L fused FFN blocks over resident weights on one device."""
+
+    def __init__(self, weights: list[LayerWeights], geo: Geometry, device, eps: float = 1e-6):
+        self.weights, self.geo, self.device, self.eps = weights, geo, torch.device(device), eps
+        self.plan = BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d, d_hidden=geo.h)
+        self._pingpong = [torch.empty(geo.seq, geo.d, device=device, dtype=torch.bfloat16) for _ in range(2)]
+        self._keep = []  # argument structs referenced by enqueued launches
+
+    def _args(self, w: LayerWeights, x, x_out, time, indices=None, cache_in=None, cache_out=None, n=0):
+        a = _lib.BlockArgs()
+        a.x = x.data_ptr()
+        a.mod = w.mod.data_ptr()
+        a.time = time.data_ptr()
+        a.time_stride = 6 * self.geo.d
+        a.w_up, a.b_up = w.w_up.data_ptr(), w.b_up.data_ptr()
+        a.w_down, a.b_down = w.w_down.data_ptr(), w.b_down.data_ptr()
+        if indices is not None:
+            a.indices = indices.data_ptr()
+            a.index_bytes = indices.element_size()
+            a.rows = indices.numel()
+        else:
+            a.rows = self.geo.seq
+        a.seq = self.geo.seq
+        a.cache_rows = n
+        a.cache_in = None if cache_in is None else cache_in.data_ptr()
+        a.cache_out = None if cache_out is None else cache_out.data_ptr()
+        a.x_out = x_out.data_ptr()
+        a.eps = self.eps
+        return a
+
+    def enqueue_pass(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
+        """Runs the L layers; with `reuse`, layers 1.. gather its indices and
+        update its history."""
+        geo = self.geo
+        src = x_in
+        for layer, w in enumerate(self.weights):
+            dst = x_final if layer == geo.layers - 1 else self._pingpong[layer % 2]
+            if reuse is not None and layer > 0:
+                a = self._args(w, src, dst, time, reuse.indices, reuse.history_in[layer - 1],
+                               reuse.history_out[layer - 1], geo.current)
+            else:
+                a = self._args(w, src, dst, time)
+            self._keep.append(a)
+            _lib.check(_lib.lib().wamffn_block_run(self.plan.handle, stream, ctypes.byref(a)))
+            src = dst
+
+    def enqueue_request(self, req: Request, stream: int) -> None:
+        self._keep.clear()
+        self.enqueue_pass(req.x[0], req.out[0], req.time[0], stream, reuse=req)   # update 0, token reuse
+        self.enqueue_pass(req.x[1], req.out[1], req.time[1], stream)              # update 3, full refresh
+
+    def launches_per_request(self) -> int:
+        return 4 * 2 * self.geo.layers
+
+    def close(self):
+        self.plan.close()
