@@ -40,10 +40,10 @@ UP_GEMM_DRAM_BYTES = None
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--requests", type=int, default=8, help="requests per GPU per step")
+    p.add_argument("--requests", type=int, default=16, help="requests per GPU per step")
     p.add_argument("--layers", type=int, default=30)
     p.add_argument("--cpu-sample-layers", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -75,7 +75,7 @@ class Clocks:
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.file, stderr=subprocess.DEVNULL, start_new_session=True)
         except Exception:
             self.proc = None
@@ -211,28 +211,36 @@ def config_dict(geo, args, world):
 def time_dominant_kernel(device, geo, pk):
     """CUDA-event timing of the up-projection GEMM (M = 392) launched alone:
     achieved TFLOP/s against the burst bf16 peak."""
-    from waminfer_b200.ffn import Plan
+    from waminfer_b200.ffn import Plan, pack_weight
 
     g = torch.Generator(device=device).manual_seed(77)
     m = geo.seq
     x = (torch.randn(m, geo.d, device=device, generator=g)).to(torch.bfloat16)
-    w = (torch.randn(geo.h, geo.d, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    w = pack_weight((torch.randn(geo.h, geo.d, device=device, generator=g) * 0.02).to(torch.bfloat16))
     b = torch.zeros(geo.h, device=device, dtype=torch.bfloat16)
     plan = Plan(x, w, b, exhaustive=False, gelu=True)
-    # Rotate over weight copies larger than L2 so every launch streams from HBM.
+    # Rotate over weight copies (4 x 88 MB > L2) so every launch streams its
+    # weights from HBM; launches are replayed from a CUDA graph so no host gap
+    # sits between them.
     ws = [w] + [w.clone() for _ in range(3)]
-    stream = torch.cuda.current_stream(device)
-    for i in range(3):
-        plan.run(x, ws[i % 4], b)
     iters = 40
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(device)
-    start.record(stream)
-    for i in range(iters):
-        plan.run(x, ws[i % 4], b)
-    end.record(stream)
-    end.synchronize()
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            plan.run(x, ws[i % 4], b)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(iters):
+                plan.run(x, ws[i % 4], b)
+        graph.replay()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+        end.synchronize()
     ms = start.elapsed_time(end) / iters
+    graph.reset()
     flops = 2 * m * geo.d * geo.h
     achieved = flops / (ms * 1e-3) / 1e12
     plan.close()
@@ -286,8 +294,9 @@ def run_ours(args, world, rank, local):
     with torch.cuda.graph(graph, stream=stream):
         for req in requests:
             stack.enqueue_request(req, handle)
-    for _ in range(args.warmup):
-        graph.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
     torch.cuda.synchronize(device)
 
     uuid = None
@@ -297,7 +306,7 @@ def run_ours(args, world, rank, local):
         pass
     barrier(world)
     torch.cuda.synchronize(device)
-    with Clocks(uuid) as clocks:
+    with Clocks(uuid) as clocks, torch.cuda.stream(stream):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):

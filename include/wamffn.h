@@ -54,6 +54,10 @@ extern "C" {
 #define WAMFFN_ERR_CAPTURE 4     /* plan creation/tuning attempted during stream capture */
 #define WAMFFN_ERR_DEVICE 5      /* a kernel reported an error through the device status word */
 
+/* Flags of wamffn_linear_plan_create. */
+#define WAMFFN_LINEAR_GELU 1     /* tanh-GELU epilogue (the up projection) */
+#define WAMFFN_WEIGHTS_PACKED 2  /* weights are in the tile-packed layout of wamffn_pack_weight */
+
 /* Bits of the device status word (wamffn_*_status). */
 #define WAMFFN_DEV_TIMEOUT 1u    /* a pipeline wait exceeded its time limit; the kernel bailed out */
 #define WAMFFN_DEV_BAD_INDEX 2u  /* a gather/scatter index was outside [-1, seq) or >= cache rows */
@@ -75,16 +79,27 @@ const char* wamffn_last_error(void);
 /* Number of kernels this library has launched in the process (all devices). */
 unsigned long long wamffn_launch_count(void);
 
+/* Phase trace of the GEMM kernels (profiling aid; no reference counterpart:
+ * the reference relies on external Nsight traces).  With a device buffer of
+ * `records` x 8 uint64 (word 0 of record 0 is the record counter, zeroed by the
+ * caller), every GEMM CTA appends {tag, start, operands ready, MMAs issued,
+ * accumulator ready, epilogue done, SM id, K blocks} in globaltimer ns.
+ * buffer == NULL switches tracing off.  Synchronous; not for use in capture. */
+int wamffn_trace_enable(int device, void* buffer, int records);
+
 /* ------------------------------------------------------------------------
  * Linear plan: y[rows, n_out] = act(x[rows, k_in] . weight[n_out, k_in]^T + bias)
- * act = tanh-GELU when gelu != 0 (no bf16 rounding between bias and GELU,
- * as in the reference's GELU_BIAS epilogue), identity otherwise.
+ * act = tanh-GELU with WAMFFN_LINEAR_GELU (no bf16 rounding between bias and
+ * GELU, as in the reference's GELU_BIAS epilogue), identity otherwise.
+ * With WAMFFN_WEIGHTS_PACKED the weight passed to run is the tile-packed copy
+ * made by wamffn_pack_weight (the reference likewise runs on a repacked copy
+ * made at prepare time, ffn.py:82-88); otherwise it is row-major [n_out, k_in].
  * fp32 accumulation, bf16 output.  Replaces Plan(...) (cpp:161-174).
  * `tune` != 0 times the candidate split-K factors on the device (like the
  * reference's exhaustive candidate timing, cpp:121-158) and keeps the fastest;
  * otherwise a static heuristic picks the configuration.
  * ---------------------------------------------------------------------- */
-int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int gelu, int tune,
+int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int flags, int tune,
                               wamffn_linear_plan** plan);
 int wamffn_linear_plan_destroy(wamffn_linear_plan* plan);
 
@@ -105,6 +120,12 @@ int wamffn_linear_status(wamffn_linear_plan* plan, uint32_t* status, int clear);
 int wamffn_ffn_run(wamffn_linear_plan* up, wamffn_linear_plan* down, void* stream, const void* x,
                    const void* w_up, const void* b_up, const void* w_down, const void* b_down,
                    void* out);
+
+/* Weight repack for HBM streaming (replaces the repack of PreparedFFN.prepare,
+ * ffn.py:82-88): dst[n_out/128][k_in/64][128][64] <- src[n_out][k_in], so that
+ * every 128 x 64 tile a GEMM CTA loads is one contiguous 16 KB block.
+ * n_out % 128 == 0, k_in % 64 == 0; src and dst hold n_out*k_in bf16. */
+int wamffn_pack_weight(void* stream, const void* src, void* dst, int n_out, int k_in);
 
 /* ------------------------------------------------------------------------
  * Modulated norm (op wam_infer::modulated_norm, _triton_inference.py:130-221)
@@ -170,6 +191,7 @@ typedef struct wamffn_block_args {
   const void* b_up;       /* [h] */
   const void* w_down;     /* [d, h] */
   const void* b_down;     /* [d] */
+  int weights_packed;     /* 1: w_up / w_down are wamffn_pack_weight copies */
   const void* indices;    /* [rows] gather list or NULL */
   int index_bytes;        /* 4 or 8 */
   int rows;               /* gathered rows M */

@@ -114,3 +114,34 @@ def ffn_block(x, update, normalized, mod, time, w_up, b_up, w_down, b_down, indi
     clean = output[:cache_rows].clone() if cache_rows > 0 else None
     x_next = gate_residual(y, output, mod, time)
     return x_next, output, clean, o
+
+
+MAX_ABS = 2e-2    # elementwise bound (or one bf16 ulp of the reference value, whichever is larger)
+MEAN_REL = 5e-3   # mean |error| / mean |reference|
+
+
+def bf16_ulp(t: torch.Tensor) -> torch.Tensor:
+    """Spacing of bfloat16 values at |t| (8 significant bits)."""
+    _, exponent = torch.frexp(t.float().abs().clamp_min(2.0**-126))
+    return torch.ldexp(torch.ones_like(t, dtype=torch.float32), exponent - 8)
+
+
+def check_close(actual: torch.Tensor, expected: torch.Tensor, max_abs: float = MAX_ABS,
+                mean_rel: float = MEAN_REL) -> tuple[bool, str]:
+    """Parity rule for bf16 outputs against the fp32 oracle: every element within
+    max(max_abs, 1 bf16 ulp of the reference) -- two correct implementations
+    that accumulate in different orders can round one ulp apart, and one ulp
+    exceeds 2e-2 above |x| = 4 -- and the mean relative error within mean_rel."""
+    a, e = actual.float().cpu(), expected.float().cpu()
+    if not bool(torch.isfinite(a).all()):
+        return False, "non-finite output"
+    err = (a - e).abs()
+    bound = torch.maximum(torch.full_like(e, max_abs), bf16_ulp(e))
+    over = err - bound
+    excess = float(over.max())
+    rel = float(err.mean() / e.abs().mean().clamp_min(1e-12))
+    ok = excess <= 0 and rel <= mean_rel
+    worst = tuple(int(i) for i in torch.nonzero(over == over.max())[0])
+    return ok, (f"max abs {float(err.max()):.4g} (worst excess over bound {excess:.3g} at {worst}: "
+                f"got {float(a[worst]):.6g}, expected {float(e[worst]):.6g}; "
+                f"{int((over > 0).sum())} elements over), mean rel {rel:.3g}")

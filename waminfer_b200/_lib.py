@@ -48,7 +48,12 @@ EXPORTED_SYMBOLS = (
     "wamffn_block_status",
     "wamffn_block_configuration",
     "wamffn_select_tokens",
+    "wamffn_pack_weight",
+    "wamffn_trace_enable",
 )
+
+LINEAR_GELU = 1
+WEIGHTS_PACKED = 2
 
 
 class NormArgs(ctypes.Structure):
@@ -88,6 +93,7 @@ class BlockArgs(ctypes.Structure):
         ("b_up", ctypes.c_void_p),
         ("w_down", ctypes.c_void_p),
         ("b_down", ctypes.c_void_p),
+        ("weights_packed", ctypes.c_int),
         ("indices", ctypes.c_void_p),
         ("index_bytes", ctypes.c_int),
         ("rows", ctypes.c_int),
@@ -149,6 +155,8 @@ def _declare(lib):
     lib.wamffn_block_status.argtypes = [vp, u32p, i]
     lib.wamffn_block_configuration.argtypes = [vp, i, u32p, i]
     lib.wamffn_select_tokens.argtypes = [vp, ctypes.POINTER(SelectArgs)]
+    lib.wamffn_pack_weight.argtypes = [vp, vp, vp, i, i]
+    lib.wamffn_trace_enable.argtypes = [i, vp, i]
     for name in EXPORTED_SYMBOLS:
         if name not in ("wamffn_last_error", "wamffn_launch_count"):
             getattr(lib, name).restype = i

@@ -123,8 +123,8 @@ def _rows2d(t: torch.Tensor, dim: int, name: str) -> torch.Tensor:
 def block_args(x, update, normalized, mod, time, w_up, b_up, w_down, b_down, indices, cache, cache_rows,
                eps, x_out, output, clean, y=None) -> _lib.BlockArgs:
     """Builds the C argument struct from torch tensors (shape/dtype checked)."""
-    d = w_up.shape[1]
-    h = w_up.shape[0]
+    packed = w_up.dim() == 4
+    h, d = (w_up.shape[0] * 128, w_up.shape[1] * 64) if packed else (w_up.shape[0], w_up.shape[1])
     x2 = _rows2d(x, d, "x")
     seq = x2.shape[0]
     if update is not None:
@@ -138,8 +138,10 @@ def block_args(x, update, normalized, mod, time, w_up, b_up, w_down, b_down, ind
     if time.ndim == 4 and time.shape[1] not in (1, seq):
         raise ValueError("per-token time must have one row per sequence row")
     for name, w, shape in (("w_up", w_up, (h, d)), ("w_down", w_down, (d, h))):
-        if w.dtype != torch.bfloat16 or tuple(w.shape) != shape or not w.is_contiguous():
-            raise ValueError(f"{name} must be a contiguous bf16 {list(shape)} (out, in) matrix")
+        want = (shape[0] // 128, shape[1] // 64, 128, 64) if packed else shape
+        if w.dtype != torch.bfloat16 or tuple(w.shape) != want or not w.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 {list(shape)} (out, in) matrix"
+                             f"{' in the packed layout' if packed else ''}")
     for name, b, n in (("b_up", b_up, h), ("b_down", b_down, d)):
         if b.dtype != torch.bfloat16 or b.numel() != n or not b.is_contiguous():
             raise ValueError(f"{name} must be a contiguous bf16 vector of {n}")
@@ -162,6 +164,7 @@ def block_args(x, update, normalized, mod, time, w_up, b_up, w_down, b_down, ind
         b_up=b_up.data_ptr(),
         w_down=w_down.data_ptr(),
         b_down=b_down.data_ptr(),
+        weights_packed=int(packed),
         indices=None if indices is None else indices.data_ptr(),
         index_bytes=0 if indices is None else indices.element_size(),
         rows=rows,
@@ -202,7 +205,7 @@ def ffn_block(
       (empty when ``cache_rows == 0``).
     """
     plan = _BLOCK_PLANS[plan_id]
-    d = w_up.shape[1]
+    d = w_up.shape[1] * 64 if w_up.dim() == 4 else w_up.shape[1]
     x_next = torch.empty_like(x)
     seq = x.numel() // d
     output = torch.empty_like(x) if want_output else x.new_empty((0,))
@@ -219,7 +222,7 @@ def ffn_block(
 @ffn_block.register_fake
 def _fake_block(x, update, normalized, mod, time, w_up, b_up, w_down, b_down, indices, cache, cache_rows, plan_id,
                 eps, want_output):
-    d = w_up.shape[1]
+    d = w_up.shape[1] * 64 if w_up.dim() == 4 else w_up.shape[1]
     output = torch.empty_like(x) if want_output else x.new_empty((0,))
     clean = x.new_empty((1, cache_rows, d)) if cache_rows > 0 else x.new_empty((0,))
     return torch.empty_like(x), output, clean
@@ -249,16 +252,41 @@ class VideoFFN:
         device = first[0].weight.device
         self.plan_id = register_block_plan(BlockPlan(device, max_rows, max_seq, self.d, self.h, tune))
         self.eps = [getattr(getattr(b, "norm2", None), "eps", 1e-6) for b in blocks]
+        self.packed = {}
+        self.signatures = {}
 
     @property
     def plan(self) -> BlockPlan:
         return _BLOCK_PLANS[self.plan_id]
 
+    def prepare(self) -> bool:
+        """Refreshes the tile-packed weight copies whose parameter signature
+        changed (the repack of ``PreparedFFN.prepare``); returns whether any did."""
+        from waminfer_b200.ffn import pack_weight
+
+        if torch.is_grad_enabled() or getattr(self.backbone, "training", False):
+            raise RuntimeError("FFN preparation requires eval mode and disabled gradients.")
+        changed = False
+        for layer_id, block in enumerate(self.backbone.dit.blocks):
+            ffn = block.ffn
+            if not isinstance(ffn[1], torch.nn.GELU) or ffn[1].approximate != "tanh":
+                raise ValueError("Fused FFN requires tanh GELU.")
+            for index in (0, 2):
+                layer = ffn[index]
+                if layer.weight.dtype != torch.bfloat16 or layer.weight.device.type != "cuda" or layer.bias is None:
+                    raise ValueError("Fused FFN requires CUDA BF16 linear layers with bias.")
+                signature = _parameter_signature(layer.weight)
+                if self.signatures.get((layer_id, index)) != signature:
+                    self.packed[layer_id, index] = pack_weight(layer.weight.detach())
+                    self.signatures[layer_id, index] = signature
+                    changed = True
+        return changed
+
     def _weights(self, layer_id):
         ffn = self.backbone.dit.blocks[layer_id].ffn
-        if not isinstance(ffn[1], torch.nn.GELU) or ffn[1].approximate != "tanh":
-            raise ValueError("Fused FFN requires tanh GELU.")
-        return ffn[0].weight, ffn[0].bias, ffn[2].weight, ffn[2].bias
+        if (layer_id, 0) not in self.packed:
+            self.prepare()
+        return self.packed[layer_id, 0], ffn[0].bias, self.packed[layer_id, 2], ffn[2].bias
 
     def _run(self, layer_id, state, x, update, normalized):
         block = self.backbone.dit.blocks[layer_id]

@@ -114,7 +114,9 @@ int prepare_device(int device, int* sm_count) {
                   device, major, minor);
     WAMFFN_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device));
     DeviceGuard g(device);
-    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemLimit));
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemLimit));
     d.ready = true;
   }
@@ -125,11 +127,17 @@ int prepare_device(int device, int* sm_count) {
 // ---------------------------------------------------------------- GEMM config
 struct GemmConfig {
   int rows = 0, n_out = 0, k_in = 0;
-  int tok_pad = 0, mma_n0 = 0, mma_n1 = 0, tok_box = 0, n_boxes = 0;
-  int stages = 0, splits = 1;
+  int group = 1;  // CTAs per UMMA (2 = cta_group::2 pair)
+  int tok_pad = 0, mma_n0 = 0, mma_n1 = 0, tok_box = 0, n_boxes = 0, b_rows = 0;
+  int a_stages = 0, b_stages = 0, splits = 1;
   uint32_t tmem_cols = 0;
   int smem_bytes = 0;
 };
+
+bool pair_enabled() {
+  static const bool on = env_flag("WAMFFN_PAIR", true);
+  return on;
+}
 
 int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c) {
   if (rows < 1 || rows > kMaxTokens)
@@ -141,30 +149,55 @@ int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c) {
   c->rows = rows;
   c->n_out = n_out;
   c->k_in = k_in;
-  c->tok_pad = (rows + 15) / 16 * 16;
-  if (c->tok_pad <= 256) {
-    c->mma_n0 = c->tok_pad;
-    c->mma_n1 = 0;
-    c->tok_box = c->tok_pad;
-    c->n_boxes = 1;
+  c->group = (pair_enabled() && (n_out / kFeatTile) % 2 == 0) ? 2 : 1;
+  if (c->group == 2) {
+    // Pair: each CTA holds half of every UMMA's tokens (multiples of 8 rows).
+    if (rows <= 256) {
+      c->tok_pad = (rows + 15) / 16 * 16;
+      c->mma_n0 = c->tok_pad;
+      c->mma_n1 = 0;
+      c->n_boxes = 1;
+      c->tok_box = c->tok_pad / 2;
+    } else {
+      c->tok_pad = (rows + 31) / 32 * 32;
+      c->mma_n0 = c->mma_n1 = c->tok_pad / 2;
+      c->n_boxes = 2;
+      c->tok_box = c->tok_pad / 4;
+    }
+    c->b_rows = c->tok_pad / 2;
   } else {
-    c->mma_n0 = (c->tok_pad / 16 + 1) / 2 * 16;
-    c->mma_n1 = c->tok_pad - c->mma_n0;
-    c->tok_box = c->tok_pad / 2;  // multiple of 8: each box starts on a 1024-byte swizzle atom
-    c->n_boxes = 2;
+    c->tok_pad = (rows + 15) / 16 * 16;
+    if (c->tok_pad <= 256) {
+      c->mma_n0 = c->tok_pad;
+      c->mma_n1 = 0;
+      c->tok_box = c->tok_pad;
+      c->n_boxes = 1;
+    } else {
+      c->mma_n0 = (c->tok_pad / 16 + 1) / 2 * 16;
+      c->mma_n1 = c->tok_pad - c->mma_n0;
+      c->tok_box = c->tok_pad / 2;  // multiple of 8: each box starts on a 1024-byte swizzle atom
+      c->n_boxes = 2;
+    }
+    c->b_rows = c->tok_pad;
   }
   uint32_t cols = 32;
   while (cols < uint32_t(c->tok_pad)) cols <<= 1;
   c->tmem_cols = cols;
-  const int stage = gemm_a_bytes() + gemm_b_bytes(c->tok_pad);
-  c->stages = (kSmemLimit - kSmemReserve) / stage;
-  if (c->stages > kMaxStages) c->stages = kMaxStages;
-  if (c->stages < 2) return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d leaves fewer than 2 pipeline stages", rows);
+  // Shared memory: the activation ring (L2 hits, needs depth against the
+  // lockstep bursts of all SMs) and the weight ring (HBM stream) share 227 KB.
+  const int budget = kSmemLimit - kSmemReserve;
+  const int b_bytes = c->b_rows * kBlockK * 2;
+  c->b_stages = (budget / 2) / b_bytes;
+  if (c->b_stages > kMaxBStages) c->b_stages = kMaxBStages;
+  if (c->b_stages < 2) c->b_stages = 2;
+  c->a_stages = (budget - c->b_stages * b_bytes) / gemm_a_bytes();
+  if (c->a_stages > kMaxAStages) c->a_stages = kMaxAStages;
+  if (c->a_stages < 2) return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d leaves fewer than 2 pipeline stages", rows);
   const int k_blocks = k_in / kBlockK;
   if (splits < 1) splits = 1;
   if (splits > k_blocks) splits = k_blocks;
   c->splits = splits;
-  c->smem_bytes = c->stages * stage + kSmemReserve;
+  c->smem_bytes = c->a_stages * gemm_a_bytes() + c->b_stages * b_bytes + kSmemReserve;
   return WAMFFN_OK;
 }
 
@@ -182,11 +215,13 @@ int default_splits(int n_out, int k_in, int sm_count) {
   return best;
 }
 
-int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* weight, const void* act,
-                const void* bias, void* out, unsigned int* status, bool pdl) {
+int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* weight, bool packed,
+                const void* act, const void* bias, void* out, unsigned int* status, bool pdl) {
   CUtensorMap tm_w, tm_x;
-  int rc = encode_operand(&tm_w, weight, uint64_t(c.k_in), uint64_t(c.n_out), uint64_t(c.k_in) * 2,
-                          kFeatTile);
+  int rc = packed ? encode_operand(&tm_w, weight, uint64_t(kBlockK), uint64_t(c.n_out) * (c.k_in / kBlockK),
+                                   uint64_t(kBlockK) * 2, kFeatTile)
+                  : encode_operand(&tm_w, weight, uint64_t(c.k_in), uint64_t(c.n_out), uint64_t(c.k_in) * 2,
+                                   kFeatTile);
   if (rc) return rc;
   rc = encode_operand(&tm_x, act, uint64_t(c.k_in), uint64_t(c.rows), uint64_t(c.k_in) * 2,
                       uint32_t(c.tok_box));
@@ -198,13 +233,15 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   p.mma_n1 = c.mma_n1;
   p.tok_box = c.tok_box;
   p.n_boxes = c.n_boxes;
+  p.b_rows = c.b_rows;
   p.k_blocks = c.k_in / kBlockK;
   p.splits = c.splits;
-  p.stages = c.stages;
+  p.a_stages = c.a_stages;
+  p.b_stages = c.b_stages;
   p.n_total = c.n_out;
   p.tmem_cols = c.tmem_cols;
   p.epi = epi;
-  p.pdl = 1;
+  p.w_packed = packed ? 1 : 0;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.out = out;
   p.status = status;
@@ -214,12 +251,17 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = size_t(c.smem_bytes);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = unsigned(c.group);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel, tm_w, tm_x, p));
+  cfg.numAttrs = 2;
+  if (c.group == 2) WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<2>, tm_w, tm_x, p));
+  else WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<1>, tm_w, tm_x, p));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;
 }
@@ -274,6 +316,7 @@ bool pdl_enabled() {
 struct wamffn_linear_plan {
   int device = 0;
   int gelu = 0;
+  int packed = 0;
   int tuned = 0;
   GemmConfig cfg;
   float* partial = nullptr;      // [splits, rows, n_out] when splits > 1
@@ -303,10 +346,11 @@ int linear_execute(wamffn_linear_plan* plan, cudaStream_t stream, const void* x,
   const GemmConfig& c = plan->cfg;
   const bool pdl = pdl_enabled();
   if (c.splits == 1) {
-    return launch_gemm(c, plan->gelu ? EPI_GELU_BF16 : EPI_BIAS_BF16, stream, weight, x, bias, out,
+    return launch_gemm(c, plan->gelu ? EPI_GELU_BF16 : EPI_BIAS_BF16, stream, weight, plan->packed, x, bias, out,
                        plan->status, pdl);
   }
-  int rc = launch_gemm(c, EPI_PARTIAL_F32, stream, weight, x, nullptr, plan->partial, plan->status, pdl);
+  int rc = launch_gemm(c, EPI_PARTIAL_F32, stream, weight, plan->packed, x, nullptr, plan->partial, plan->status,
+                       pdl);
   if (rc) return rc;
   EpiParams e{};
   e.partial = plan->partial;
@@ -358,7 +402,7 @@ const char* wamffn_last_error(void) { return g_error.c_str(); }
 
 unsigned long long wamffn_launch_count(void) { return g_launches.load(); }
 
-int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int gelu, int tune,
+int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int flags, int tune,
                               wamffn_linear_plan** out_plan) {
   if (!out_plan) return fail(WAMFFN_ERR_INVALID, "plan output pointer is null");
   *out_plan = nullptr;
@@ -379,7 +423,8 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int gel
   }
   auto* plan = new wamffn_linear_plan();
   plan->device = device;
-  plan->gelu = gelu ? 1 : 0;
+  plan->gelu = (flags & WAMFFN_LINEAR_GELU) ? 1 : 0;
+  plan->packed = (flags & WAMFFN_WEIGHTS_PACKED) ? 1 : 0;
   rc = make_gemm_config(rows, n_out, k_in, default_splits(n_out, k_in, sm), &plan->cfg);
   if (rc) {
     delete plan;
@@ -465,8 +510,8 @@ int wamffn_linear_run(wamffn_linear_plan* plan, void* stream, const void* x, con
 int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values, int n) {
   if (!plan || !values) return fail(WAMFFN_ERR_INVALID, "null argument");
   const GemmConfig& c = plan->cfg;
-  const uint32_t v[7] = {uint32_t(kFeatTile), uint32_t(c.tok_pad), uint32_t(c.mma_n1 > 0 ? 2 : 1),
-                         uint32_t(c.stages),   uint32_t(c.splits),  c.tmem_cols,
+  const uint32_t v[7] = {uint32_t(kFeatTile * c.group), uint32_t(c.tok_pad), uint32_t(c.mma_n1 > 0 ? 2 : 1),
+                         uint32_t(c.a_stages * 100 + c.b_stages), uint32_t(c.splits), c.tmem_cols,
                          uint32_t(plan->tuned)};
   for (int i = 0; i < n && i < 7; ++i) values[i] = v[i];
   return WAMFFN_OK;
@@ -659,12 +704,12 @@ int wamffn_block_run(wamffn_block_plan* plan, void* stream_, const wamffn_block_
   rc = launch_norm(n, a->seq > a->rows ? a->seq : a->rows, stream, pdl);
   if (rc) return rc;
   // 2. up projection + bias + GELU -> hidden.
-  rc = launch_gemm(up, EPI_GELU_BF16, stream, a->w_up, plan->gathered, a->b_up, plan->hidden,
-                   plan->status, pdl);
+  rc = launch_gemm(up, EPI_GELU_BF16, stream, a->w_up, a->weights_packed != 0, plan->gathered, a->b_up,
+                   plan->hidden, plan->status, pdl);
   if (rc) return rc;
   // 3. down projection, split-K fp32 partials.
-  rc = launch_gemm(down, EPI_PARTIAL_F32, stream, a->w_down, plan->hidden, nullptr, plan->partial,
-                   plan->status, pdl);
+  rc = launch_gemm(down, EPI_PARTIAL_F32, stream, a->w_down, a->weights_packed != 0, plan->hidden, nullptr,
+                   plan->partial, plan->status, pdl);
   if (rc) return rc;
   // 4. reduce + bias, scatter into the cache, gated residual.
   EpiParams e{};
@@ -706,10 +751,37 @@ int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t
   const GemmConfig* cs[2] = {&up, &down};
   int k = 0;
   for (const GemmConfig* c : cs) {
-    const uint32_t v[7] = {uint32_t(kFeatTile), uint32_t(c->tok_pad), uint32_t(c->mma_n1 > 0 ? 2 : 1),
-                           uint32_t(c->stages),  uint32_t(c->splits),  c->tmem_cols, 0u};
+    const uint32_t v[7] = {uint32_t(kFeatTile * c->group), uint32_t(c->tok_pad), uint32_t(c->mma_n1 > 0 ? 2 : 1),
+                           uint32_t(c->a_stages * 100 + c->b_stages), uint32_t(c->splits), c->tmem_cols, 0u};
     for (int i = 0; i < 7 && k < n; ++i) values[k++] = v[i];
   }
+  return WAMFFN_OK;
+}
+
+int wamffn_trace_enable(int device, void* buffer, int records) {
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", device);
+  if (buffer && (records < 2 || !aligned16(buffer))) return fail(WAMFFN_ERR_INVALID, "trace buffer too small");
+  unsigned long long* ptr = static_cast<unsigned long long*>(buffer);
+  unsigned int cap = buffer ? unsigned(records) : 0u;
+  WAMFFN_CUDA(cudaMemcpyToSymbol(g_trace, &ptr, sizeof(ptr)));
+  WAMFFN_CUDA(cudaMemcpyToSymbol(g_trace_capacity, &cap, sizeof(cap)));
+  return WAMFFN_OK;
+}
+
+int wamffn_pack_weight(void* stream, const void* src, void* dst, int n_out, int k_in) {
+  if (!src || !dst) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (n_out < kFeatTile || n_out % kFeatTile || k_in < kBlockK || k_in % kBlockK)
+    return fail(WAMFFN_ERR_INVALID, "pack needs n_out %% 128 == 0 and k_in %% 64 == 0 (got %d, %d)", n_out, k_in);
+  if (!aligned16(src) || !aligned16(dst)) return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
+  if (src == dst) return fail(WAMFFN_ERR_INVALID, "pack cannot run in place");
+  const long long vectors = (long long)n_out * k_in / 8;
+  int blocks = int((vectors + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  pack_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n_out, k_in);
+  WAMFFN_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;
 }
 

@@ -3,58 +3,96 @@
 // out[t, f] = epilogue( sum_k act[t, k] * weight[f, k] )
 //
 // The problem is "swap-AB": the weight rows (output features) sit on the UMMA
-// M axis (128 per CTA) and the few hundred activation rows (tokens) sit on the
-// UMMA N axis, so one CTA holds every token of its 128 features in TMEM
-// (<= 512 fp32 columns) and each weight tile is read from HBM exactly once.
-// Operands are staged by TMA with the 128-byte swizzle, K-major on both sides
+// M axis and the few hundred activation rows (tokens) sit on the UMMA N axis,
+// so a CTA holds every token of its 128 features in TMEM (<= 512 fp32
+// columns) and each weight tile is read from HBM exactly once.  Operands are
+// staged by TMA with the 128-byte swizzle, K-major on both sides
 // (torch.nn.Linear's native [out, in] weight layout and row-major activations).
 //
-// Roles (320 threads):
-//   warp 0      TMA producer (one elected lane)
-//   warp 1      TMEM allocator + UMMA issuer (one elected lane)
-//   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4).., columns split
-//               between the two warpgroups
-// Grid: (n_total / 128, split_k).  With split_k > 1 each CTA covers a
-// contiguous range of K blocks and writes an fp32 partial; a row kernel sums
-// the partials in split order (deterministic, no atomics).
+// kGroup == 2 (the default for an even number of 128-feature tiles) runs the
+// 2-SM UMMA: a cluster of two CTAs computes 256 features; each CTA stages its
+// own 128 weight rows and HALF of the activation rows, the leader issues
+// tcgen05.mma.cta_group::2 (M = 256) over both CTAs' shared memory, and each
+// CTA's TMEM receives its 128 features x all tokens.  Every activation tile
+// therefore crosses L2 once per 256 features instead of once per 128, and each
+// SM buffers half as many activation bytes per stage.  No load uses cluster
+// multicast: each CTA loads its own operands; only the MMA-completion commit
+// is multicast to both CTAs' barriers.
+//
+// The two operands travel through separate shared-memory rings: a ring for
+// the 16 KB weight tiles (HBM stream) and a ring for the activation tiles
+// (re-read by every CTA pair, L2 hits).  Weights do not depend on the previous
+// kernel, so under programmatic dependent launch the weight producer starts
+// streaming before the previous kernel has finished; only the activation
+// producer waits for it.
+//
+// Roles (384 threads per CTA):
+//   warp 0      weight (A) TMA producer, one lane
+//   warp 1      TMEM allocator + UMMA issuer (leader CTA), one lane
+//   warp 2      activation (B) TMA producer, one lane
+//   warp 3      idle
+//   warps 4..11 epilogue: warp w reads TMEM lanes 32*(w%4).., the two
+//               warpgroups take alternate 16-column chunks
+// Grid: (n_total / 128, split_k), clusters of (kGroup, 1, 1).  With
+// split_k > 1 each CTA covers a contiguous range of K blocks and writes an
+// fp32 partial; a row kernel sums the partials in split order
+// (deterministic, no atomics).
 #pragma once
 
 #include "ptx.cuh"
+#include "wamffn.h"
 
 namespace wamffn {
 
 enum : int { EPI_GELU_BF16 = 0, EPI_BIAS_BF16 = 1, EPI_PARTIAL_F32 = 2 };
 
-constexpr int kFeatTile = 128;         // UMMA M
+constexpr int kFeatTile = 128;         // feature rows per CTA (UMMA M per CTA)
 constexpr int kBlockK = 64;            // bf16 elements per 128-byte swizzled row
-constexpr int kGemmThreads = 320;
+constexpr int kGemmThreads = 384;
+constexpr int kEpiWarp0 = 4;           // first epilogue warp
 constexpr int kMaxTokens = 512;        // TMEM holds 512 fp32 columns
-constexpr int kMaxStages = 8;
+constexpr int kMaxAStages = 16;
+constexpr int kMaxBStages = 8;
 constexpr int kSmemLimit = 232448;     // 227 KB opt-in dynamic shared memory
-constexpr int kSmemReserve = 1024 + 256;  // alignment slack + barriers
+constexpr int kSmemReserve = 1024 + 512;  // alignment slack + barriers
 
 struct GemmParams {
   int tokens;        // real activation rows
-  int tok_pad;       // tokens rounded up to 16
+  int tok_pad;       // tokens rounded up to the MMA granularity
   int mma_n0;        // N of the first UMMA (<= 256, multiple of 16)
   int mma_n1;        // N of the second UMMA (0 when one suffices)
-  int tok_box;       // activation rows per TMA box
+  int tok_box;       // activation rows per TMA box (per CTA)
   int n_boxes;       // TMA boxes per stage for the activation tile
+  int b_rows;        // activation rows per stage held by one CTA
   int k_blocks;      // K / 64
   int splits;        // split-K factor == gridDim.y
-  int stages;        // pipeline depth
+  int a_stages;      // weight ring depth
+  int b_stages;      // activation ring depth
   int n_total;       // output features (row length of the output)
   uint32_t tmem_cols;
   int epi;
-  int pdl;           // 1: wait on the previous grid before reading activations
+  int w_packed;      // weights in the tile-packed layout (one 16 KB block per tile)
   const __nv_bfloat16* bias;
   void* out;
   unsigned int* status;
 };
 
 __host__ __device__ constexpr int gemm_a_bytes() { return kFeatTile * kBlockK * 2; }
-__host__ __device__ inline int gemm_b_bytes(int tok_pad) { return tok_pad * kBlockK * 2; }
 
+// Optional phase trace (off unless wamffn_trace_enable registered a buffer):
+// record = {tag, start, operands ready, MMAs issued, accumulator ready,
+// epilogue done, sm id, k blocks}; globaltimer nanoseconds.
+constexpr int kTraceWords = 8;
+__device__ unsigned long long* g_trace = nullptr;
+__device__ unsigned int g_trace_capacity = 0;
+
+__device__ __forceinline__ uint32_t smid() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+  return r;
+}
+
+template <int kGroup>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                      const GemmParams p) {
@@ -63,108 +101,206 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kGroup == 2 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
 
   const int a_bytes = gemm_a_bytes();
-  const int b_bytes = gemm_b_bytes(p.tok_pad);
+  const int b_bytes = p.b_rows * kBlockK * 2;
   uint8_t* a_base = smem;
-  uint8_t* b_base = smem + p.stages * a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.stages * (a_bytes + b_bytes));
-  uint64_t* full = bars;
-  uint64_t* empty = bars + p.stages;
-  uint64_t* tmem_full = bars + 2 * p.stages;
+  uint8_t* b_base = smem + p.a_stages * a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + p.b_stages * b_bytes);
+  uint64_t* full_a = bars;
+  uint64_t* empty_a = full_a + p.a_stages;
+  uint64_t* full_b = empty_a + p.a_stages;
+  uint64_t* empty_b = full_b + p.b_stages;
+  uint64_t* tmem_full = empty_b + p.b_stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  unsigned int* trace_slot = reinterpret_cast<unsigned int*>(tmem_slot + 2);
 
-  const int n0 = blockIdx.x * kFeatTile;
+  const int n0 = blockIdx.x * kFeatTile;  // this CTA's feature rows
   const int split = blockIdx.y;
   const int kb0 = int((long long)p.k_blocks * split / p.splits);
   const int kb1 = int((long long)p.k_blocks * (split + 1) / p.splits);
   const int nkb = kb1 - kb0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.stages; ++s) {
-      mbar_init(smem_addr(&full[s]), 1);
-      mbar_init(smem_addr(&empty[s]), 1);
+    for (int s = 0; s < p.a_stages; ++s) {
+      mbar_init(smem_addr(&full_a[s]), 1);
+      mbar_init(smem_addr(&empty_a[s]), 1);
+    }
+    for (int s = 0; s < p.b_stages; ++s) {
+      mbar_init(smem_addr(&full_b[s]), 1);
+      mbar_init(smem_addr(&empty_b[s]), 1);
     }
     mbar_init(smem_addr(tmem_full), 1);
     *abort_flag = 0;
+    *trace_slot = 0xffffffffu;
+    if (g_trace != nullptr) {
+      const unsigned int slot = atomicAdd(reinterpret_cast<unsigned int*>(g_trace), 1u);
+      if (slot + 1 < g_trace_capacity) {
+        *trace_slot = slot + 1;
+        unsigned long long* rec = g_trace + size_t(slot + 1) * kTraceWords;
+        rec[0] = (unsigned long long)(blockIdx.x | (blockIdx.y << 16)) | ((unsigned long long)p.epi << 32);
+        rec[1] = globaltimer_ns();
+        rec[6] = smid();
+        rec[7] = (unsigned long long)(kb1 - kb0);
+      }
+    }
     fence_mbar_init();
     prefetch_tensormap(&tm_w);
     prefetch_tensormap(&tm_x);
   }
   if (warp == 1) {
-    tmem_alloc(smem_addr(tmem_slot), p.tmem_cols);
-    tmem_relinquish();
+    tmem_alloc_g<kGroup>(smem_addr(tmem_slot), p.tmem_cols);
+    tmem_relinquish_g<kGroup>();
   }
   tc_fence_before();
-  __syncthreads();
+  // Both CTAs' barriers must be initialised before either signals the other.
+  if constexpr (kGroup == 2) cluster_sync();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ producer
-      const uint64_t pol_w = l2_policy_evict_first();  // weights stream once
-      const uint64_t pol_x = l2_policy_evict_last();   // activations are re-read by every CTA
-      const uint32_t stage_tx = uint32_t(a_bytes + b_bytes);
-      if (p.pdl) pdl_wait_prior();
-      int issued = 0;
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const uint32_t ph = uint32_t(i / p.stages) & 1u;
-        if (!wait_bounded(smem_addr(&empty[s]), ph ^ 1u, abort_flag, p.status, 1u)) break;
-        const uint32_t fb = smem_addr(&full[s]);
-        mbar_arrive_expect_tx(fb, stage_tx);
+  if (warp == 0 || warp == 2) {
+    // -------------------------------------------------------------- producers
+    // The whole warp runs the loop (warp-uniform operands); one elected lane
+    // issues the barrier arrive and the TMA copies.
+    const bool weights = warp == 0;
+    const int stages = weights ? p.a_stages : p.b_stages;
+    uint64_t* full = weights ? full_a : full_b;
+    uint64_t* empty = weights ? empty_a : empty_b;
+    uint8_t* ring = weights ? a_base : b_base;
+    const int bytes = weights ? a_bytes : b_bytes;
+    // Weights stream once (evict first); activations are re-read by every CTA.
+    const uint64_t policy = weights ? l2_policy_evict_first() : l2_policy_evict_last();
+    // Only the activations depend on the previous kernel in the stream.
+    if (!weights) pdl_wait_prior();
+    int issued = 0;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % stages;
+      const uint32_t ph = uint32_t(i / stages) & 1u;
+      // One lane polls; the verdict is broadcast so the warp stays converged.
+      int ok = 1;
+      if (lane == 0) ok = wait_bounded(smem_addr(&empty[s]), ph ^ 1u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      if (elect_one()) {
+        const uint32_t local_full = smem_addr(&full[s]);
+        // The leader's barrier counts both CTAs' bytes; the peer only adds its copies.
+        const uint32_t fb = kGroup == 2 ? map_to_cta(local_full, 0) : local_full;
+        if (leader) mbar_arrive_expect_tx(local_full, uint32_t(bytes * kGroup));
         const int kx = (kb0 + i) * kBlockK;
-        tma_load_2d(smem_addr(a_base + s * a_bytes), &tm_w, fb, kx, n0, pol_w);
-        for (int b = 0; b < p.n_boxes; ++b)
-          tma_load_2d(smem_addr(b_base + s * b_bytes + b * p.tok_box * kBlockK * 2), &tm_x, fb, kx,
-                      b * p.tok_box, pol_x);
-        issued = i + 1;
+        if (weights) {
+          // Packed weights: tile (feature tile, k block) is rows [t*128, t*128+128) of a [*, 64] matrix.
+          const int c0 = p.w_packed ? 0 : kx;
+          const int c1 = p.w_packed ? (blockIdx.x * p.k_blocks + kb0 + i) * kFeatTile : n0;
+          if constexpr (kGroup == 2) tma_load_2d_pair(smem_addr(ring + s * bytes), &tm_w, fb, c0, c1, policy);
+          else tma_load_2d(smem_addr(ring + s * bytes), &tm_w, fb, c0, c1, policy);
+        } else {
+          for (int b = 0; b < p.n_boxes; ++b) {
+            const uint32_t dst = smem_addr(ring + s * bytes + b * p.tok_box * kBlockK * 2);
+            if constexpr (kGroup == 2) {
+              // Box b feeds UMMA b: this CTA holds its rank's half of that UMMA's tokens.
+              tma_load_2d_pair(dst, &tm_x, fb, kx, b * (2 * p.tok_box) + int(rank) * p.tok_box, policy);
+            } else {
+              tma_load_2d(dst, &tm_x, fb, kx, b * p.tok_box, policy);
+            }
+          }
+        }
       }
-      if (*abort_flag) {
-        // Let the copies already in flight land before the CTA releases its shared memory.
-        const int first = issued > p.stages ? issued - p.stages : 0;
-        for (int i = first; i < issued; ++i)
-          wait_drain(smem_addr(&full[i % p.stages]), uint32_t(i / p.stages) & 1u);
+      __syncwarp();
+      issued = i + 1;
+    }
+    if (*abort_flag && lane == 0) {
+      // Let the copies already in flight land before the CTA releases its
+      // shared memory (the peer's copies complete on the leader's barrier,
+      // so the peer just waits a bounded moment).
+      if (kGroup == 1 || leader) {
+        const int first = issued > stages ? issued - stages : 0;
+        for (int i = first; i < issued; ++i) wait_drain(smem_addr(&full[i % stages]), uint32_t(i / stages) & 1u);
+      } else {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000ll) {
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ UMMA issuer
-      const uint32_t idesc0 = umma_idesc_bf16(kFeatTile, p.mma_n0);
-      const uint32_t idesc1 = umma_idesc_bf16(kFeatTile, p.mma_n1 > 0 ? p.mma_n1 : 16);
+    // -------------------------------------------------------------- UMMA issuer
+    // The whole warp runs the loop; the elected lane issues the MMAs and the
+    // commits (a commit tracks the MMAs issued by the same thread).
+    if (leader) {
+      unsigned long long* rec =
+          *trace_slot != 0xffffffffu ? g_trace + size_t(*trace_slot) * kTraceWords : nullptr;
+      const int m = kFeatTile * kGroup;
+      const uint32_t idesc0 = umma_idesc_bf16(m, p.mma_n0);
+      const uint32_t idesc1 = umma_idesc_bf16(m, p.mma_n1 > 0 ? p.mma_n1 : 16);
+      // Rows of UMMA 0's activation slice held by this CTA.
+      const uint32_t b1_offset = uint32_t(p.mma_n0 / kGroup) * 128u;
+      const uint32_t a0 = smem_addr(a_base), b0 = smem_addr(b_base);
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages;
-        const uint32_t ph = uint32_t(i / p.stages) & 1u;
-        if (!wait_bounded(smem_addr(&full[s]), ph, abort_flag, p.status, 1u)) break;
+        const int sa = i % p.a_stages, sb = i % p.b_stages;
+        int ok = 1;
+        if (lane == 0)
+          ok = wait_bounded(smem_addr(&full_a[sa]), uint32_t(i / p.a_stages) & 1u, abort_flag, p.status,
+                            WAMFFN_DEV_TIMEOUT) &&
+               wait_bounded(smem_addr(&full_b[sb]), uint32_t(i / p.b_stages) & 1u, abort_flag, p.status,
+                            WAMFFN_DEV_TIMEOUT);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         tc_fence_after();
-        const uint32_t a_addr = smem_addr(a_base + s * a_bytes);
-        const uint32_t b_addr = smem_addr(b_base + s * b_bytes);
-        const uint64_t adesc = umma_desc_sw128(a_addr);
-        const uint64_t bdesc0 = umma_desc_sw128(b_addr);
-        const uint64_t bdesc1 = umma_desc_sw128(b_addr + uint32_t(p.mma_n0) * 128u);
+        if (i == 0 && rec && lane == 0) rec[2] = globaltimer_ns();
+        const uint64_t adesc = umma_desc_sw128(a0 + uint32_t(sa * a_bytes));
+        const uint64_t bdesc0 = umma_desc_sw128(b0 + uint32_t(sb * b_bytes));
+        const uint64_t bdesc1 = umma_desc_sw128(b0 + uint32_t(sb * b_bytes) + b1_offset);
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < kBlockK / 16; ++k) {
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-          umma_bf16(tmem_base, adesc + 2 * k, bdesc0 + 2 * k, idesc0, acc);
-          if (p.mma_n1 > 0)
-            umma_bf16(tmem_base + uint32_t(p.mma_n0), adesc + 2 * k, bdesc1 + 2 * k, idesc1, acc);
+          for (int k = 0; k < kBlockK / 16; ++k) {
+            const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+            if constexpr (kGroup == 2) {
+              umma_bf16_pair(tmem_base, adesc + 2 * k, bdesc0 + 2 * k, idesc0, acc);
+              if (p.mma_n1 > 0)
+                umma_bf16_pair(tmem_base + uint32_t(p.mma_n0), adesc + 2 * k, bdesc1 + 2 * k, idesc1, acc);
+            } else {
+              umma_bf16(tmem_base, adesc + 2 * k, bdesc0 + 2 * k, idesc0, acc);
+              if (p.mma_n1 > 0)
+                umma_bf16(tmem_base + uint32_t(p.mma_n0), adesc + 2 * k, bdesc1 + 2 * k, idesc1, acc);
+            }
+          }
+          // Free both stages (in both CTAs) once these MMAs have read them.
+          if constexpr (kGroup == 2) {
+            umma_commit_pair(smem_addr(&empty_a[sa]), 0x3);
+            umma_commit_pair(smem_addr(&empty_b[sb]), 0x3);
+          } else {
+            umma_commit(smem_addr(&empty_a[sa]));
+            umma_commit(smem_addr(&empty_b[sb]));
+          }
         }
-        umma_commit(smem_addr(&empty[s]));  // frees the stage once these MMAs have read it
+        __syncwarp();
       }
-      umma_commit(smem_addr(tmem_full));    // accumulator complete (or pipeline aborted)
+      // Accumulator complete (or pipeline aborted): release the epilogues.
+      if (elect_one()) {
+        if constexpr (kGroup == 2) umma_commit_pair(smem_addr(tmem_full), 0x3);
+        else umma_commit(smem_addr(tmem_full));
+      }
+      __syncwarp();
+      if (rec && lane == 0) rec[3] = globaltimer_ns();
     }
-  } else {
+    // The next kernel may start its prologue (and its weight stream) now.
+    if (lane == 0) pdl_launch_dependents();
+  } else if (warp >= kEpiWarp0) {
     // -------------------------------------------------------------- epilogue
+    const int ew = warp - kEpiWarp0;      // 0..7
     const int q = warp & 3;               // TMEM lane quarter this warp may access
-    const int half = (warp - 2) >> 2;     // which half of the column chunks
+    const int half = ew >> 2;             // which half of the column chunks
     // One lane waits; the verdict is broadcast so the .sync.aligned TMEM loads
     // below are executed by all 32 lanes or by none.
     int ok = 0;
-    if (lane == 0) ok = wait_bounded(smem_addr(tmem_full), 0u, abort_flag, p.status, 1u) && !*abort_flag;
+    if (lane == 0)
+      ok = wait_bounded(smem_addr(tmem_full), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT) && !*abort_flag;
     ok = __shfl_sync(0xffffffffu, ok, 0);
     tc_fence_after();
+    unsigned long long* rec =
+        (ew == 0 && lane == 0 && *trace_slot != 0xffffffffu) ? g_trace + size_t(*trace_slot) * kTraceWords : nullptr;
+    if (rec) rec[4] = globaltimer_ns();
     if (ok) {
       const int f_local = q * 32 + lane;
       const int f = n0 + f_local;
@@ -184,9 +320,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else {
         // bf16 output through a per-warp shared-memory transpose so that each
-        // thread writes 16 contiguous bytes of one token row.
+        // thread writes 16 contiguous bytes of one token row.  The weight ring
+        // is idle once the accumulator is complete, so its first 8 KB hold the
+        // transpose tiles.
         const float bias = __bfloat162float(p.bias[f]);
-        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + (warp - 2) * (16 * 32);
+        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + ew * (16 * 32);
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
         const int n_base = n0 + q * 32;
         for (int c = half; c < nchunks; c += 2) {
@@ -213,12 +351,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   }
-  if (threadIdx.x == 0) pdl_launch_dependents();
+  if (warp == kEpiWarp0 && lane == 0 && *trace_slot != 0xffffffffu)
+    g_trace[size_t(*trace_slot) * kTraceWords + 5] = globaltimer_ns();
   tc_fence_before();
-  __syncthreads();
+  // No CTA of a pair may leave while its peer can still signal its barriers.
+  if constexpr (kGroup == 2) cluster_sync();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    tmem_dealloc_g<kGroup>(tmem_base, p.tmem_cols);
   }
 }
 

@@ -12,7 +12,11 @@
 namespace wamffn {
 
 // Time limit of any single pipeline wait.  Healthy waits take microseconds.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+// Measured with the SM cycle counter (%clock64 is a register read; the
+// %globaltimer uncore read is far slower and would sit on the critical path of
+// every pipeline stage): 4e9 cycles is 2-4 s at 1-2 GHz.
+constexpr long long kWaitLimitCycles = 4000000000ll;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, for waits outside pipelines
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -22,6 +26,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// One lane of a converged warp is elected (the same lane every time for a
+// fully active warp).  Issuing tcgen05/TMA instructions from elected lanes of a
+// warp that runs the loop as a whole keeps their operands warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, %1;\n\t"
+      "@px mov.s32 %0, 1;\n\t}\n"
+      : "+r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
 }
 
 // ---------------------------------------------------------------- mbarrier
@@ -35,6 +53,34 @@ __device__ __forceinline__ void fence_mbar_init() {
 
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Non-blocking probe of a phase (cheap when the phase is already complete,
+// which is the common case in a well-fed pipeline).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Blocking probe: the thread sleeps until the phase completes or about
+// `hint_ns` elapse (no busy polling of the barrier unit meanwhile).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -60,12 +106,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 // device status word.  Returns true on success.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort,
                                              unsigned int* status, unsigned int timeout_bit) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (clock64() - t0 > kWaitLimitCycles) {
       *abort = 1;
       if (status) atomicOr(status, timeout_bit);
       return false;
@@ -75,9 +121,9 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
 
 // Same wait without the abort shortcut, used to drain in-flight copies.
 __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if (clock64() - t0 > kWaitLimitCycles) return false;
   }
   return true;
 }
@@ -110,7 +156,84 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Same load issued by one CTA of a 2-SM pair (.cta_group::2): `bar` may be the
+// peer (leader) CTA's barrier in the shared::cluster window.  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Cluster-wide barrier (all threads of all CTAs of the cluster).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
+template <int kGroup>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t dst_smem, uint32_t ncols) {
+  if constexpr (kGroup == 2)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+  else
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+}
+
+template <int kGroup>
+__device__ __forceinline__ void tmem_relinquish_g() {
+  if constexpr (kGroup == 2)
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  else
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+template <int kGroup>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+  if constexpr (kGroup == 2)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  else
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// 2-SM UMMA issued by the pair's leader: D (+)= A * B^T with A split by rows
+// and B split by columns across the two CTAs' shared memory (same offsets).
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` (same offset) in every CTA of `cta_mask` once the pair's
+// previously issued MMAs completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
                "r"(ncols)
@@ -201,12 +324,31 @@ __device__ __forceinline__ void pdl_wait_prior() {
 }
 
 // ---------------------------------------------------------------- math
-// tanh-approximated GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-// (Hendrycks & Gimpel, 2016), evaluated in fp32 with the CUDA tanhf.
+// tanh-approximated GELU, 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3)
+// (Hendrycks & Gimpel, 2016), evaluated in fp32 through the identity
+// 1 + tanh(u) = 2 / (1 + e^{-2u}), i.e. gelu = x / (1 + 2^{-2 u log2 e}),
+// with the hardware base-2 exponential and reciprocal (relative error ~1e-6,
+// far below the bf16 rounding of the result).
+__device__ __forceinline__ float ex2_approx(float v) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  const float inner = k0 * (x + k1 * x * x * x);
+  const float c = -2.0f * 0.7978845608028654f * 1.4426950408889634f;  // -2 sqrt(2/pi) log2(e)
+  const float t = ex2_approx(c * fmaf(k1 * x, x * x, x));
+  return x * rcp_approx(1.0f + t);
+}
+
+// Reference form with the CUDA tanhf, used by the accuracy self-test.
+__device__ __forceinline__ float gelu_tanh_precise(float x) {
+  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
   return 0.5f * x * (1.0f + tanhf(inner));
 }
 

@@ -300,4 +300,19 @@ __global__ void __launch_bounds__(kRowThreads) rowepi_kernel(const EpiParams p) 
   if (tid == 0) pdl_launch_dependents();
 }
 
+// Weight repack: dst[n/128][k/64][128][64] <- src[n][k] (16-byte vectors;
+// stores are contiguous, each group of 8 threads reads 128 contiguous bytes).
+__global__ void pack_weight_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int n_out, int k_in) {
+  const long long kb_count = k_in / 64;
+  const long long total = (long long)n_out * k_in / 8;
+  for (long long v = blockIdx.x * (long long)blockDim.x + threadIdx.x; v < total;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long c8 = v & 7;
+    const long long r = (v >> 3) & 127;
+    const long long kb = (v >> 10) % kb_count;
+    const long long nt = (v >> 10) / kb_count;
+    dst[v] = src[((nt * 128 + r) * k_in + kb * 64) / 8 + c8];
+  }
+}
+
 }  // namespace wamffn

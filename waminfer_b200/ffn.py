@@ -10,9 +10,10 @@ with cuBLASLt replaced by libwamffn's tcgen05 GEMMs:
 * the down projection is split-K with a deterministic reduction + bias.
 
 Plans and their workspaces are owned per model, never process-wide
-(``WAMInfer/ffn.py:5-6``).  Weights are used in torch.nn.Linear's native
-[out, in] layout (K-major for the kernels), so no repacked copy is kept unless
-a weight is not contiguous.
+(``WAMInfer/ffn.py:5-6``).  Like the reference, ``prepare`` keeps a repacked
+copy of every weight, refreshed when the parameter's signature changes; the
+copy is tile-packed ([out/128, in/64, 128, 64]) so that the GEMMs stream each
+128 x 64 weight tile as one contiguous 16 KB block from HBM.
 """
 
 from __future__ import annotations
@@ -33,6 +34,26 @@ def _stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def packed_shape(n_out: int, k_in: int) -> tuple[int, int, int, int]:
+    return (n_out // 128, k_in // 64, 128, 64)
+
+
+def pack_weight(weight: torch.Tensor) -> torch.Tensor:
+    """Tile-packed copy of an [out, in] bf16 weight: [out/128, in/64, 128, 64],
+    so every 128 x 64 tile a GEMM CTA streams is one contiguous 16 KB block
+    (``wamffn_pack_weight``; the reference makes its repacked copy at the same
+    point, ``WAMInfer/ffn.py:82-88``)."""
+    if weight.dim() != 2 or weight.dtype != torch.bfloat16 or not weight.is_cuda:
+        raise ValueError("pack_weight expects a CUDA bf16 [out, in] matrix")
+    n_out, k_in = weight.shape
+    src = weight.contiguous()
+    dst = torch.empty(packed_shape(n_out, k_in), dtype=weight.dtype, device=weight.device)
+    with torch.cuda.device(weight.device):
+        _lib.check(_lib.lib().wamffn_pack_weight(_stream_handle(weight.device), src.data_ptr(), dst.data_ptr(),
+                                                 n_out, k_in))
+    return dst
+
+
 class Plan:
     """One linear GEMM plan on one device (replaces ``Plan`` of
     ``WAMInfer/_cublaslt_inference.cpp:41-190``).
@@ -43,22 +64,28 @@ class Plan:
     graph capture (``cpp:167-168``).
     """
 
-    def __init__(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, exhaustive: bool, gelu: bool = False):
+    def __init__(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, exhaustive: bool, gelu: bool = False,
+                 packed: bool | None = None):
         if not (x.is_cuda and weight.device == x.device and bias.device == x.device):
             raise RuntimeError("Plan tensors must share one CUDA device")
         if not (x.dtype == torch.bfloat16 and weight.dtype == x.dtype and bias.dtype == x.dtype):
             raise RuntimeError("Plan tensors must be bfloat16")
-        if not (x.dim() == 2 and weight.dim() == 2 and bias.dim() == 1 and bias.numel() == weight.shape[0]
-                and weight.shape[1] == x.shape[1]):
+        if packed is None:
+            packed = weight.dim() == 4
+        n = weight.shape[0] * 128 if packed else weight.shape[0]
+        k = weight.shape[1] * 64 if packed else weight.shape[1]
+        if not (x.dim() == 2 and bias.dim() == 1 and bias.numel() == n and k == x.shape[1]):
             raise RuntimeError("Plan shapes do not form x[m,k] . weight[n,k]^T + bias[n]")
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("GEMM tuning must finish before CUDA Graph capture")
-        self.m, self.n, self.k = x.shape[0], weight.shape[0], x.shape[1]
+        self.m, self.n, self.k = x.shape[0], n, k
         self.gelu = bool(gelu)
+        self.packed = bool(packed)
         self.device = x.device
+        flags = (_lib.LINEAR_GELU if self.gelu else 0) | (_lib.WEIGHTS_PACKED if self.packed else 0)
         handle = ctypes.c_void_p()
         _lib.check(_lib.lib().wamffn_linear_plan_create(
-            x.device.index, self.m, self.n, self.k, int(self.gelu), int(bool(exhaustive)), ctypes.byref(handle)))
+            x.device.index, self.m, self.n, self.k, flags, int(bool(exhaustive)), ctypes.byref(handle)))
         self._handle = handle
 
     def run(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
@@ -72,7 +99,10 @@ class Plan:
             raise RuntimeError("tensors must be bfloat16")
         if not (x.is_contiguous() and x.dim() == 2 and x.shape[0] == self.m and x.shape[1] == self.k):
             raise RuntimeError(f"x must be contiguous [{self.m}, {self.k}]")
-        if not (weight.dim() == 2 and weight.shape == (self.n, self.k) and weight.stride() == (self.k, 1)):
+        if self.packed:
+            if not (weight.is_contiguous() and tuple(weight.shape) == packed_shape(self.n, self.k)):
+                raise RuntimeError(f"weight must be the packed copy of a [{self.n}, {self.k}] matrix")
+        elif not (weight.dim() == 2 and weight.shape == (self.n, self.k) and weight.stride() == (self.k, 1)):
             raise RuntimeError(f"weight must be a contiguous [{self.n}, {self.k}] (out, in) matrix")
         if not (bias.is_contiguous() and bias.numel() == self.n):
             raise RuntimeError("bias must be contiguous with one entry per output feature")
@@ -113,7 +143,8 @@ def prepared_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, p
 
 @prepared_linear.register_fake
 def _fake_linear(x, weight, bias, plan_id):
-    return torch.empty((x.shape[0], weight.shape[0]), dtype=x.dtype, device=x.device)
+    n = weight.shape[0] * 128 if weight.dim() == 4 else weight.shape[0]
+    return torch.empty((x.shape[0], n), dtype=x.dtype, device=x.device)
 
 
 class PreparedFFN:
@@ -135,7 +166,8 @@ class PreparedFFN:
         if key not in self.keys:
             if len(self.keys) >= self.max_plans:
                 raise RuntimeError("FFN preparation supports at most 32 device/shape plans per model.")
-            x = torch.empty(rows, weight.shape[1], device=weight.device, dtype=weight.dtype)
+            k = weight.shape[1] * 64 if weight.dim() == 4 else weight.shape[1]
+            x = torch.empty(rows, k, device=weight.device, dtype=weight.dtype)
             plan = Plan(x, weight, bias, True, gelu)
             plan_id = next(_IDS)
             _PLANS[plan_id] = plan
@@ -160,8 +192,7 @@ class PreparedFFN:
                 key = (layer_id, index)
                 signature = _parameter_signature(layer.weight)
                 if self.signatures.get(key) != signature:
-                    weight = layer.weight.detach()
-                    self.weights[key] = weight if weight.is_contiguous() else weight.contiguous()
+                    self.weights[key] = pack_weight(layer.weight.detach())
                     self.signatures[key] = signature
                     changed = True
                 packed.append(self.weights[key])

@@ -111,19 +111,26 @@ class FFNStack:
     """L fused FFN blocks over resident weights on one device."""
 
     def __init__(self, weights: list[LayerWeights], geo: Geometry, device, eps: float = 1e-6):
+        from waminfer_b200.ffn import pack_weight
+
         self.weights, self.geo, self.device, self.eps = weights, geo, torch.device(device), eps
+        # Tile-packed copies streamed by the GEMMs (one contiguous 16 KB block per tile).
+        self.packed = [(pack_weight(w.w_up), pack_weight(w.w_down)) for w in weights]
         self.plan = BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d, d_hidden=geo.h)
         self._pingpong = [torch.empty(geo.seq, geo.d, device=device, dtype=torch.bfloat16) for _ in range(2)]
         self._keep = []  # argument structs referenced by enqueued launches
 
-    def _args(self, w: LayerWeights, x, x_out, time, indices=None, cache_in=None, cache_out=None, n=0):
+    def _args(self, layer: int, x, x_out, time, indices=None, cache_in=None, cache_out=None, n=0):
+        w = self.weights[layer]
+        w_up, w_down = self.packed[layer]
         a = _lib.BlockArgs()
         a.x = x.data_ptr()
         a.mod = w.mod.data_ptr()
         a.time = time.data_ptr()
         a.time_stride = 6 * self.geo.d
-        a.w_up, a.b_up = w.w_up.data_ptr(), w.b_up.data_ptr()
-        a.w_down, a.b_down = w.w_down.data_ptr(), w.b_down.data_ptr()
+        a.w_up, a.b_up = w_up.data_ptr(), w.b_up.data_ptr()
+        a.w_down, a.b_down = w_down.data_ptr(), w.b_down.data_ptr()
+        a.weights_packed = 1
         if indices is not None:
             a.indices = indices.data_ptr()
             a.index_bytes = indices.element_size()
@@ -143,13 +150,13 @@ class FFNStack:
         update its history."""
         geo = self.geo
         src = x_in
-        for layer, w in enumerate(self.weights):
+        for layer in range(len(self.weights)):
             dst = x_final if layer == geo.layers - 1 else self._pingpong[layer % 2]
             if reuse is not None and layer > 0:
-                a = self._args(w, src, dst, time, reuse.indices, reuse.history_in[layer - 1],
+                a = self._args(layer, src, dst, time, reuse.indices, reuse.history_in[layer - 1],
                                reuse.history_out[layer - 1], geo.current)
             else:
-                a = self._args(w, src, dst, time)
+                a = self._args(layer, src, dst, time)
             self._keep.append(a)
             _lib.check(_lib.lib().wamffn_block_run(self.plan.handle, stream, ctypes.byref(a)))
             src = dst
