@@ -33,8 +33,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "FFN-stack ms/request and TFLOP/s (2F, 32/120 reuse) at 1/2/4/8 B200; % bf16 roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one up-projection launch at
-# M = 392 from the committed ncu capture (profiles/umma_gemm_up_m392.md); None until captured.
-UP_GEMM_DRAM_BYTES = None
+# M = 392 from the committed ncu capture (profiles/umma_gemm_ffn_m392.md):
+# 90.56 MB read + 2.95 MB written.
+UP_GEMM_DRAM_BYTES = 93_512_000
 
 
 def parse():
@@ -48,6 +49,7 @@ def parse():
     p.add_argument("--cpu-sample-layers", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-gpu-baselines", action="store_true")
     return p.parse_args()
 
 
@@ -146,7 +148,7 @@ def max_over_ranks(value: float, world: int, device) -> float:
 
 
 # ------------------------------------------------------------------ CPU side
-def cpu_baseline(geo, sample_layers: int):
+def cpu_baseline(geo, sample_layers: int, min_seconds: float = 10.0):
     """The reference's native CPU FFN path (Linear -> GELU(tanh) -> Linear in
     bf16, gather/scatter/gate in torch) restated by the oracle, timed on all
     host cores over a bounded sample: `sample_layers` reuse layers (M = 304)
@@ -156,7 +158,7 @@ def cpu_baseline(geo, sample_layers: int):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    flops, seconds = cpu_path.time_layers(geo, sample_layers)
+    flops, seconds = cpu_path.time_layers(geo, sample_layers, min_seconds=min_seconds)
     per_request_s = seconds / flops * geo.request_flops()
     return {
         "value": flops / seconds / 1e12,
@@ -177,11 +179,13 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     geo = Geometry(layers=args.layers)
+    # Each step is a bounded sample (about 3 s of CPU work) so that the whole
+    # --steps K --warmup W run stays within a few minutes.
     for _ in range(max(0, min(args.warmup, 1))):
-        cpu_baseline(geo, 1)
+        cpu_baseline(geo, 1, min_seconds=0.5)
     values = []
     for _ in range(args.steps):
-        values.append(cpu_baseline(geo, args.cpu_sample_layers))
+        values.append(cpu_baseline(geo, 1, min_seconds=3.0))
     value = statistics.median(v["value"] for v in values)
     base = values[0]
     ms = geo.request_flops() / (value * 1e12) * 1e3
@@ -252,6 +256,82 @@ def time_dominant_kernel(device, geo, pk):
         "traffic": UP_GEMM_DRAM_BYTES,
         "algorithmic_bytes": 2 * (geo.h * geo.d + m * geo.d + m * geo.h),
     }
+
+
+def _graph_ms_per_replay(fn, device, replays):
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+    ms = start.elapsed_time(end) / replays
+    graph.reset()
+    return ms
+
+
+def gpu_baselines(device, geo, weights, replays=5):
+    """Same-GPU baselines over one request's 60 layer passes (FFN GEMMs only,
+    no norm / gather / scatter), CUDA-graph replayed:
+    * torch native Linear -> GELU(tanh) -> Linear (what the reference runs on
+      B200, WAMInfer/blocks.py:254-258);
+    * the reference's own cuBLASLt prepared path (WAMInfer/ffn.py:96-107 over
+      WAMInfer/_cublaslt_inference.cpp Plan, exhaustive tuning, col-major weight
+      copies), built by baseline/build_reference_cublaslt.py."""
+    import torch.nn.functional as F
+
+    out = {}
+    g = torch.Generator(device=device).manual_seed(99)
+    rows = geo.request_rows()
+    xs = {m: torch.randn(m, geo.d, device=device, generator=g).to(torch.bfloat16) for m in set(rows)}
+    layers = len(weights)
+
+    def native():
+        for i, m in enumerate(rows):
+            w = weights[i % layers]
+            h = F.gelu(F.linear(xs[m], w.w_up, w.b_up), approximate="tanh")
+            F.linear(h, w.w_down, w.b_down)
+
+    out["torch_native_ms_per_request"] = _graph_ms_per_replay(native, device, replays)
+    ref_dir = ROOT / "baseline" / "_ref"
+    if (ref_dir / "wam_infer_ffn_v1.so").exists():
+        try:
+            sys.path.insert(0, str(ref_dir))
+            import wam_infer_ffn_v1 as ext  # noqa: F401
+
+            col = [(w.w_up.T.contiguous().T, w.w_down.T.contiguous().T) for w in weights]
+            plans = {}
+            for m in set(rows):
+                h = torch.randn(m, geo.h, device=device, generator=g).to(torch.bfloat16)
+                plans[m] = (ext.Plan(xs[m], col[0][0], weights[0].b_up, True, True),
+                            ext.Plan(h, col[0][1], weights[0].b_down, True, False))
+
+            def cublaslt():
+                for i, m in enumerate(rows):
+                    w, (wu, wd) = weights[i % layers], col[i % layers]
+                    up, down = plans[m]
+                    down.run(up.run(xs[m], wu, w.b_up), wd, w.b_down)
+
+            out["reference_cublaslt_ms_per_request"] = _graph_ms_per_replay(cublaslt, device, replays)
+            out["reference_cublaslt_configs"] = {str(m): [list(p.selected_configuration()) for p in plans[m]]
+                                                 for m in plans}
+            del col, plans
+        except Exception as exc:  # reported, not fatal: the product arm does not depend on it
+            out["reference_cublaslt_error"] = f"{type(exc).__name__}: {exc}"
+    else:
+        out["reference_cublaslt_error"] = "baseline/_ref/wam_infer_ffn_v1.so not built"
+    torch.cuda.synchronize(device)
+    return out
 
 
 def request_roofline_ms(geo, pk):
@@ -363,6 +443,13 @@ def run_ours(args, world, rank, local):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(geo, args.cpu_sample_layers)
+    baselines = None
+    if rank == 0 and world == 1 and not args.no_gpu_baselines:
+        baselines = gpu_baselines(device, geo, weights)
+        baselines["ours_ms_per_request"] = ms_request
+        for key in ("torch_native", "reference_cublaslt"):
+            if f"{key}_ms_per_request" in baselines:
+                baselines[f"speedup_vs_{key}"] = baselines[f"{key}_ms_per_request"] / ms_request
 
     launches = stack.launches_per_request() * args.requests * args.steps
     if rank == 0:
@@ -373,7 +460,7 @@ def run_ours(args, world, rank, local):
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
             "config": config_dict(geo, args, world),
             "request_roofline_ms": roof_ms, "request_roofline_frac": roof_ms / ms_request,
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_baselines": baselines,
             "gpu_launches": launches, "launches_per_request": stack.launches_per_request(),
             "library_launches_total": _lib.launch_count(),
         }

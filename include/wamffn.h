@@ -5,9 +5,9 @@
  * (passed as void*), returns an int status (WAMFFN_OK == 0) and never throws.
  * On failure wamffn_last_error() returns a thread-local message.  No entry
  * point allocates device memory or synchronises the stream except the
- * *_create / *_destroy / *_tune / wamffn_*_status calls, so every run call can
- * be captured into a CUDA graph (the reference forbids tuning during capture,
- * _cublaslt_inference.cpp:167-168; *_create here refuses the same way).
+ * *_create / *_destroy / wamffn_*_status / wamffn_trace_enable calls, so every
+ * run call can be captured into a CUDA graph (the reference forbids tuning
+ * during capture, _cublaslt_inference.cpp:167-168; *_create refuses the same way).
  *
  * Tensors are bf16 (uint16 storage), row-major, last dimension contiguous.
  * Weights use torch.nn.Linear's native [out_features, in_features] layout.
@@ -215,6 +215,48 @@ int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear);
 /* {up: feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned,
  *  down: same 7 values} for a given row count. */
 int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t* values, int n);
+
+/* ------------------------------------------------------------------------
+ * FFN stack: the FFN phases of `layers` consecutive DiT layers in one call,
+ * the way the reference's 30-layer loop runs them (joint.py:93-156 with
+ * blocks.py:246-272): layers below first_gathered_layer recompute every row
+ * (the reference's layer 0, blocks.py:248); later layers gather `indices`
+ * (the same list for every layer, select_tokens, approximation.py:55-67) and
+ * read / write the history slice [layer - first_gathered_layer] of
+ * cache_in / cache_out ([layers - first_gathered_layer, cache_rows, d], the
+ * packed cache of runtime.py:263).  Between layers the split-K reduction,
+ * history scatter, gated residual and the next layer's norm + gather run as
+ * one kernel.  No attention runs between the FFNs: every layer's norm input
+ * is the previous layer's residual (update = NULL).
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_layer_weights {
+  const void* w_up;     /* [h, d] or packed */
+  const void* b_up;     /* [h] */
+  const void* w_down;   /* [d, h] or packed */
+  const void* b_down;   /* [d] */
+  const void* mod;      /* [6, d] block.modulation */
+} wamffn_layer_weights;
+
+typedef struct wamffn_stack_args {
+  int layers;
+  const wamffn_layer_weights* weights;  /* host array of `layers` entries */
+  int weights_packed;
+  const void* x;          /* [seq, d] residual entering the first layer */
+  const void* time;       /* [seq, 6, d] per-token time modulation, or [6, d] */
+  int64_t time_stride;
+  int seq;
+  const void* indices;    /* gather list of the gathered layers, or NULL (all rows) */
+  int index_bytes;
+  int rows;               /* entries of indices */
+  int first_gathered_layer;
+  int cache_rows;
+  const void* cache_in;   /* [layers - first_gathered_layer, cache_rows, d] or NULL */
+  void* cache_out;        /* same shape, or NULL */
+  void* x_out;            /* [seq, d] residual after the last layer */
+  float eps;
+} wamffn_stack_args;
+
+int wamffn_stack_run(wamffn_block_plan* plan, void* stream, const wamffn_stack_args* args);
 
 /* ------------------------------------------------------------------------
  * Token selection (select_tokens, approximation.py:55-67):

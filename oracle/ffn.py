@@ -30,7 +30,7 @@ def modulated_norm(x, update, mod, previous, time, weight, bias, mode: int, eps:
     Returns (y, norm), both bf16-valued fp32 [S, d].
     """
     x = x.float()
-    if mode > 0:
+    if mode > 0 and update is not None:  # the fused block allows no update (FFN slots on x itself)
         u = update.float()
         if mode == SELF_RESIDUAL:
             u = bf16(modulation(mod, time, 2) * u)          # :155-157

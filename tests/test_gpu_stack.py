@@ -1,0 +1,83 @@
+"""GPU: the fused multi-layer FFN stack (wamffn_stack_run).
+
+* equals the per-layer fused blocks (wamffn_block_run chained layer by layer)
+  bit for bit -- the layer boundary kernel computes the same bf16 values;
+* follows the oracle over a short stack with token reuse and history.
+"""
+
+import pytest
+import torch
+
+from oracle import ffn as offn
+
+pytestmark = pytest.mark.gpu
+
+
+def _small_geo(layers=3):
+    from waminfer_b200.stack import Geometry
+
+    return Geometry(layers=layers)
+
+
+def test_stack_equals_chained_blocks(cuda_device):
+    from waminfer_b200.stack import FFNStack, Request, make_weights
+
+    geo = _small_geo(3)
+    weights = make_weights(geo.layers, geo.d, geo.h, cuda_device, seed=3)
+    stack = FFNStack(weights, geo, cuda_device)
+    req = Request(geo, cuda_device, seed=5)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    fused_out = torch.empty_like(req.out[0])
+    stack.enqueue_pass(req.x[0], fused_out, req.time[0], stream, reuse=req)
+    fused_hist = req.history_out.clone()
+    chained_out = torch.empty_like(req.out[0])
+    stack.enqueue_pass_blocks(req.x[0], chained_out, req.time[0], stream, reuse=req)
+    torch.cuda.synchronize()
+    assert torch.equal(fused_out, chained_out)
+    assert torch.equal(fused_hist, req.history_out)
+    # full refresh as well
+    stack.enqueue_pass(req.x[1], fused_out, req.time[1], stream)
+    stack.enqueue_pass_blocks(req.x[1], chained_out, req.time[1], stream)
+    torch.cuda.synchronize()
+    assert torch.equal(fused_out, chained_out)
+    assert stack.plan.status() == 0
+    stack.close()
+
+
+def test_stack_follows_oracle_with_reuse(cuda_device):
+    from waminfer_b200.stack import FFNStack, Request, make_weights
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    geo = _small_geo(3)
+    weights = make_weights(geo.layers, geo.d, geo.h, cuda_device, seed=4)
+    stack = FFNStack(weights, geo, cuda_device)
+    req = Request(geo, cuda_device, seed=6)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    stack.enqueue_pass(req.x[0], req.out[0], req.time[0], stream, reuse=req)
+    torch.cuda.synchronize()
+
+    # Oracle: layer 0 full, layers 1.. gathered with the request's indices.
+    # Both chains carry their own residual, so differences of one bf16 ulp
+    # compound over the layers: the bound is 6e-2 (or one ulp) per element,
+    # with the same 5e-3 mean-relative bound (single layers are checked at
+    # 2e-2 in test_gpu_kernels.py).
+    x = req.x[0].float().cpu()
+    time = req.time[0].float().cpu()
+    idx = req.indices.cpu()
+    for layer, w in enumerate(weights):
+        reuse = layer > 0
+        cache = req.history_in[layer - 1].float().cpu() if reuse else None
+        x_next, output, clean, _ = offn.ffn_block(
+            x, None, None, w.mod[0].float().cpu(), time, w.w_up, w.b_up, w.w_down, w.b_down,
+            idx if reuse else None, cache, geo.current if reuse else 0, 1e-6,
+            ffn=lambda a, wu, bu, wd, bd: offn.prepared_ffn(a.to(wu.device), wu, bu, wd, bd).cpu())
+        if reuse:
+            got = req.history_out[layer - 1]
+            ok, msg = offn.check_close(got, clean, max_abs=6e-2)
+            assert ok, f"history layer {layer}: {msg}"
+            kept = sorted(set(range(geo.current)) - set(idx[: geo.count].tolist()))
+            assert torch.equal(got[kept].cpu(), req.history_in[layer - 1][kept].cpu())
+        x = x_next
+    ok, msg = offn.check_close(req.out[0], x, max_abs=6e-2)
+    assert ok, f"stack output: {msg}"
+    stack.close()

@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "wamffn_select_tokens",
     "wamffn_pack_weight",
     "wamffn_trace_enable",
+    "wamffn_stack_run",
 )
 
 LINEAR_GELU = 1
@@ -125,6 +126,41 @@ class SelectArgs(ctypes.Structure):
     ]
 
 
+class LayerWeights(ctypes.Structure):
+    """Mirror of ``wamffn_layer_weights``."""
+
+    _fields_ = [
+        ("w_up", ctypes.c_void_p),
+        ("b_up", ctypes.c_void_p),
+        ("w_down", ctypes.c_void_p),
+        ("b_down", ctypes.c_void_p),
+        ("mod", ctypes.c_void_p),
+    ]
+
+
+class StackArgs(ctypes.Structure):
+    """Mirror of ``wamffn_stack_args``."""
+
+    _fields_ = [
+        ("layers", ctypes.c_int),
+        ("weights", ctypes.POINTER(LayerWeights)),
+        ("weights_packed", ctypes.c_int),
+        ("x", ctypes.c_void_p),
+        ("time", ctypes.c_void_p),
+        ("time_stride", ctypes.c_int64),
+        ("seq", ctypes.c_int),
+        ("indices", ctypes.c_void_p),
+        ("index_bytes", ctypes.c_int),
+        ("rows", ctypes.c_int),
+        ("first_gathered_layer", ctypes.c_int),
+        ("cache_rows", ctypes.c_int),
+        ("cache_in", ctypes.c_void_p),
+        ("cache_out", ctypes.c_void_p),
+        ("x_out", ctypes.c_void_p),
+        ("eps", ctypes.c_float),
+    ]
+
+
 class WamffnError(RuntimeError):
     """A libwamffn entry point returned a non-zero status."""
 
@@ -157,6 +193,7 @@ def _declare(lib):
     lib.wamffn_select_tokens.argtypes = [vp, ctypes.POINTER(SelectArgs)]
     lib.wamffn_pack_weight.argtypes = [vp, vp, vp, i, i]
     lib.wamffn_trace_enable.argtypes = [i, vp, i]
+    lib.wamffn_stack_run.argtypes = [vp, vp, ctypes.POINTER(StackArgs)]
     for name in EXPORTED_SYMBOLS:
         if name not in ("wamffn_last_error", "wamffn_launch_count"):
             getattr(lib, name).restype = i

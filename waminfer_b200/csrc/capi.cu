@@ -734,6 +734,119 @@ int wamffn_block_run(wamffn_block_plan* plan, void* stream_, const wamffn_block_
   return launch_epi(e, stream, pdl);
 }
 
+int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_args* a) {
+  if (!plan || !a || !a->weights) return fail(WAMFFN_ERR_INVALID, "null argument");
+  if (a->layers < 1) return fail(WAMFFN_ERR_INVALID, "layers=%d", a->layers);
+  if (a->seq < 1 || a->seq > plan->max_seq || a->seq > plan->max_rows)
+    return fail(WAMFFN_ERR_INVALID, "seq=%d outside [1, %d]", a->seq, plan->max_seq < plan->max_rows ? plan->max_seq : plan->max_rows);
+  const bool gather = a->indices != nullptr && a->first_gathered_layer < a->layers;
+  if (gather && (a->rows < 1 || a->rows > plan->max_rows))
+    return fail(WAMFFN_ERR_INVALID, "rows=%d outside [1, %d]", a->rows, plan->max_rows);
+  if (gather && a->index_bytes != 4 && a->index_bytes != 8)
+    return fail(WAMFFN_ERR_INVALID, "index_bytes must be 4 or 8");
+  if (a->first_gathered_layer < 0) return fail(WAMFFN_ERR_INVALID, "first_gathered_layer < 0");
+  if (a->cache_rows < 0 || a->cache_rows > a->seq)
+    return fail(WAMFFN_ERR_INVALID, "cache_rows=%d outside [0, seq]", a->cache_rows);
+  if (gather && a->cache_rows > 0 && !a->cache_in)
+    return fail(WAMFFN_ERR_INVALID, "gathered layers with cache rows need cache_in");
+  if (!a->x || !a->time || !a->x_out) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (a->time_stride % 8) return fail(WAMFFN_ERR_INVALID, "time_stride must be a multiple of 8");
+  for (int l = 0; l < a->layers; ++l) {
+    const wamffn_layer_weights& w = a->weights[l];
+    const void* ptrs[] = {w.w_up, w.b_up, w.w_down, w.b_down, w.mod};
+    for (const void* q : ptrs)
+      if (!q || !aligned16(q)) return fail(WAMFFN_ERR_INVALID, "layer %d: null or unaligned weight", l);
+  }
+  const void* ptrs[] = {a->x, a->time, a->cache_in, a->cache_out, a->x_out};
+  for (const void* q : ptrs)
+    if (q && !aligned16(q)) return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
+  DeviceGuard guard(plan->device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", plan->device);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const bool pdl = pdl_enabled();
+  const int d = plan->d;
+  const size_t layer_cache = size_t(a->cache_rows) * d;
+  auto gathered_layer = [&](int l) { return gather && l >= a->first_gathered_layer; };
+  auto layer_rows = [&](int l) { return gathered_layer(l) ? a->rows : a->seq; };
+
+  // Prologue of the first layer: y = x, norm + gather into the activation buffer.
+  NormParams n{};
+  n.x = static_cast<const __nv_bfloat16*>(a->x);
+  n.xs = d;
+  n.mod = static_cast<const __nv_bfloat16*>(a->weights[0].mod);
+  n.time = static_cast<const __nv_bfloat16*>(a->time);
+  n.ts = a->time_stride;
+  n.y = plan->y;
+  n.rows = a->seq;
+  n.dim = d;
+  n.mode = WAMFFN_CROSS_RESIDUAL;
+  n.eps = a->eps;
+  n.idx = gathered_layer(0) ? a->indices : nullptr;
+  n.idx_bytes = a->index_bytes;
+  n.m = layer_rows(0);
+  n.gathered = plan->gathered;
+  n.pos_of_row = plan->pos;
+  n.status = plan->status;
+  n.pdl = 1;
+  int rc = launch_norm(n, a->seq > n.m ? a->seq : n.m, stream, pdl);
+  if (rc) return rc;
+  for (int l = 0; l < a->layers; ++l) {
+    const wamffn_layer_weights& w = a->weights[l];
+    const int rows = layer_rows(l);
+    GemmConfig up, down;
+    rc = block_configs(plan, rows, &up, &down);
+    if (rc) return rc;
+    rc = launch_gemm(up, EPI_GELU_BF16, stream, w.w_up, a->weights_packed != 0, plan->gathered, w.b_up, plan->hidden,
+                     plan->status, pdl);
+    if (rc) return rc;
+    rc = launch_gemm(down, EPI_PARTIAL_F32, stream, w.w_down, a->weights_packed != 0, plan->hidden, nullptr,
+                     plan->partial, plan->status, pdl);
+    if (rc) return rc;
+    BoundaryParams b{};
+    b.partial = plan->partial;
+    b.splits = down.splits;
+    b.m = rows;
+    b.dim = d;
+    b.seq = a->seq;
+    b.bias = static_cast<const __nv_bfloat16*>(w.b_down);
+    b.pos = gathered_layer(l) ? plan->pos : nullptr;
+    if (gathered_layer(l)) {
+      const size_t slot = size_t(l - a->first_gathered_layer) * layer_cache;
+      b.cache_rows = a->cache_rows;
+      b.cache_in = a->cache_in ? static_cast<const __nv_bfloat16*>(a->cache_in) + slot : nullptr;
+      b.cache_out = a->cache_out ? static_cast<__nv_bfloat16*>(a->cache_out) + slot : nullptr;
+    }
+    b.y = plan->y;
+    b.mod = static_cast<const __nv_bfloat16*>(w.mod);
+    b.time = static_cast<const __nv_bfloat16*>(a->time);
+    b.ts = a->time_stride;
+    const bool last = l + 1 == a->layers;
+    b.next_mod = last ? nullptr : static_cast<const __nv_bfloat16*>(a->weights[l + 1].mod);
+    b.next_idx = (!last && gathered_layer(l + 1)) ? a->indices : nullptr;
+    b.next_idx_bytes = a->index_bytes;
+    b.next_m = last ? 0 : layer_rows(l + 1);
+    b.next_gathered = plan->gathered;
+    b.next_pos = plan->pos;
+    b.x_final = static_cast<__nv_bfloat16*>(a->x_out);
+    b.eps = a->eps;
+    b.status = plan->status;
+    cudaLaunchConfig_t cfg{};
+    const int grid = a->seq > b.next_m ? a->seq : b.next_m;
+    cfg.gridDim = dim3(unsigned(grid), 1, 1);
+    cfg.blockDim = dim3(unsigned(row_threads(d)), 1, 1);
+    cfg.dynamicSmemBytes = size_t(d) * sizeof(float);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, boundary_kernel, b));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+  }
+  return WAMFFN_OK;
+}
+
 int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear) {
   if (!plan || !status) return fail(WAMFFN_ERR_INVALID, "null argument");
   DeviceGuard guard(plan->device);

@@ -31,8 +31,8 @@
 //   warp 1      TMEM allocator + UMMA issuer (leader CTA), one lane
 //   warp 2      activation (B) TMA producer, one lane
 //   warp 3      idle
-//   warps 4..11 epilogue: warp w reads TMEM lanes 32*(w%4).., the two
-//               warpgroups take alternate 16-column chunks
+//   epilogue    all 12 warps once their roles are done: warp w reads TMEM
+//               lanes 32*(w%4).. and every third 32-column chunk
 // Grid: (n_total / 128, split_k), clusters of (kGroup, 1, 1).  With
 // split_k > 1 each CTA covers a contiguous range of K blocks and writes an
 // fp32 partial; a row kernel sums the partials in split order
@@ -286,11 +286,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // The next kernel may start its prologue (and its weight stream) now.
     if (lane == 0) pdl_launch_dependents();
-  } else if (warp >= kEpiWarp0) {
-    // -------------------------------------------------------------- epilogue
-    const int ew = warp - kEpiWarp0;      // 0..7
+  }
+
+  // ---------------------------------------------------------------- epilogue
+  // All 12 warps (producer and issuer warps join once their loops are done):
+  // warp w reads TMEM lanes 32*(w%4).. (its 32 features) and takes every third
+  // 32-column (token) chunk, starting at chunk w/4.
+  {
     const int q = warp & 3;               // TMEM lane quarter this warp may access
-    const int half = ew >> 2;             // which half of the column chunks
+    const int group = warp >> 2;          // 0..2
     // One lane waits; the verdict is broadcast so the .sync.aligned TMEM loads
     // below are executed by all 32 lanes or by none.
     int ok = 0;
@@ -299,35 +303,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ok = __shfl_sync(0xffffffffu, ok, 0);
     tc_fence_after();
     unsigned long long* rec =
-        (ew == 0 && lane == 0 && *trace_slot != 0xffffffffu) ? g_trace + size_t(*trace_slot) * kTraceWords : nullptr;
+        (warp == kEpiWarp0 && lane == 0 && *trace_slot != 0xffffffffu) ? g_trace + size_t(*trace_slot) * kTraceWords
+                                                                       : nullptr;
     if (rec) rec[4] = globaltimer_ns();
     if (ok) {
-      const int f_local = q * 32 + lane;
-      const int f = n0 + f_local;
-      const int nchunks = (p.tokens + 15) >> 4;
+      const int f = n0 + q * 32 + lane;
+      const int nchunks = (p.tokens + 31) >> 5;
       const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
       if (p.epi == EPI_PARTIAL_F32) {
-        float* out = reinterpret_cast<float*>(p.out) + size_t(split) * p.tokens * p.n_total;
-        for (int c = half; c < nchunks; c += 2) {
-          uint32_t r[16];
-          tmem_ld16(lane_addr + uint32_t(c * 16), r);
+        // Partials are re-read once by the split-K reduction: keep them in L2.
+        const uint64_t keep = l2_policy_evict_last();
+        float* out = reinterpret_cast<float*>(p.out) + size_t(split) * p.tokens * p.n_total + f;
+        for (int c = group; c < nchunks; c += 3) {
+          uint32_t r[32];
+          tmem_ld32(lane_addr + uint32_t(c * 32), r);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int t = c * 16 + i;
-            if (t < p.tokens) out[size_t(t) * p.n_total + f] = __uint_as_float(r[i]);
+          for (int i = 0; i < 32; ++i) {
+            const int t = c * 32 + i;
+            if (t < p.tokens) st_global_keep(out + size_t(t) * p.n_total, __uint_as_float(r[i]), keep);
           }
         }
       } else {
         // bf16 output through a per-warp shared-memory transpose so that each
         // thread writes 16 contiguous bytes of one token row.  The weight ring
-        // is idle once the accumulator is complete, so its first 8 KB hold the
-        // transpose tiles.
+        // is idle once the accumulator is complete, so its first 24 KB hold the
+        // transpose tile of every warp.
         const float bias = __bfloat162float(p.bias[f]);
-        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + ew * (16 * 32);
+        __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem) + warp * (32 * 32);
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out);
         const int n_base = n0 + q * 32;
-        for (int c = half; c < nchunks; c += 2) {
+        // 16-column chunks: the GELU math keeps 16 values in flight per thread
+        // (32 measured slower: the longer dependency chains do not overlap).
+        const int nchunks16 = (p.tokens + 15) >> 4;
+        for (int c = group; c < nchunks16; c += 3) {
           uint32_t r[16];
           tmem_ld16(lane_addr + uint32_t(c * 16), r);
           tmem_wait_ld();

@@ -300,6 +300,165 @@ __global__ void __launch_bounds__(kRowThreads) rowepi_kernel(const EpiParams p) 
   if (tid == 0) pdl_launch_dependents();
 }
 
+// Layer boundary of an FFN stack: the split-K reduction + bias of layer l's
+// down projection, the scatter into layer l's history, the gated residual,
+// and -- fused on the same row -- layer l+1's LayerNorm / adaLN (FFN shift and
+// scale slots) and its row gather.  This is the reference's cross-layer fold
+// (the FFN_RESIDUAL norm of WAMInfer/_triton_inference.py:158-176 that
+// consumes the deferred FFN output of WAMInfer/blocks.py:269-271) with the
+// next layer's FFN prologue in place of its attention prologue.
+struct BoundaryParams {
+  const float* partial;         // [splits, m, dim] fp32 partials of layer l
+  int splits;
+  int m;
+  int dim;
+  int seq;
+  const __nv_bfloat16* bias;    // b_down of layer l
+  const int* pos;               // [seq] gather position of layer l, or null (identity)
+  int cache_rows;
+  const __nv_bfloat16* cache_in;
+  __nv_bfloat16* cache_out;
+  __nv_bfloat16* y;             // [seq, dim] residual of layer l, overwritten by layer l+1's
+  const __nv_bfloat16* mod;     // [6, dim] of layer l (gate slot 5)
+  const __nv_bfloat16* time;
+  long long ts;
+  const __nv_bfloat16* next_mod;  // [6, dim] of layer l+1, or null: l is the last layer
+  const void* next_idx;         // gather list of layer l+1, or null (identity)
+  int next_idx_bytes;
+  int next_m;
+  __nv_bfloat16* next_gathered; // [next_m, dim]
+  int* next_pos;                // [seq]
+  __nv_bfloat16* x_final;       // [seq, dim], written after the last layer
+  float eps;
+  unsigned int* status;
+};
+
+// Dynamic shared memory: dim floats.
+__global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryParams p) {
+  extern __shared__ float xrow[];
+  __shared__ float red[32];
+  __shared__ int matches[kMaxMatches];
+  __shared__ int n_match;
+  __shared__ int last_match;
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nvec = p.dim >> 3;
+  pdl_wait_prior();
+
+  const bool last = p.next_mod == nullptr;
+  if (!last && p.next_idx != nullptr && b < p.next_m) {
+    const long long r = load_index(p.next_idx, p.next_idx_bytes, b);
+    if (r < 0 || r >= p.seq) {
+      if (r != -1 && tid == 0) atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+      for (int v = tid; v < nvec; v += blockDim.x)
+        *reinterpret_cast<uint4*>(p.next_gathered + size_t(b) * p.dim + v * 8) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  if (b >= p.seq) return;
+  const int row = b;
+
+  // Gather slots of the next layer that read this row.
+  if (tid == 0) {
+    n_match = 0;
+    last_match = -1;
+  }
+  __syncthreads();
+  if (!last) {
+    if (p.next_idx == nullptr) {
+      if (tid == 0 && row < p.next_m) {
+        matches[0] = row;
+        n_match = 1;
+        last_match = row;
+      }
+    } else {
+      for (int j = tid; j < p.next_m; j += blockDim.x) {
+        if (load_index(p.next_idx, p.next_idx_bytes, j) == row) {
+          const int slot = atomicAdd(&n_match, 1);
+          if (slot < kMaxMatches) matches[slot] = j;
+          else atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+          atomicMax(&last_match, j);
+        }
+      }
+    }
+  }
+
+  // 1. Layer l: reduce, bias, scatter into the history, gated residual.
+  int j = p.pos != nullptr ? p.pos[row] : row;
+  if (j >= p.m) j = -1;
+  const bool cached_row = row < p.cache_rows;
+  if (j < 0 && !cached_row && tid == 0) atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+  float local = 0.f;
+  for (int v = tid; v < nvec; v += blockDim.x) {
+    const int e = v * 8;
+    float o[8];
+    if (j >= 0) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int s = 0; s < p.splits; ++s) {
+        const float4* src = reinterpret_cast<const float4*>(p.partial + (size_t(s) * p.m + j) * p.dim + e);
+        const float4 a = src[0], c = src[1];
+        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        acc[4] += c.x; acc[5] += c.y; acc[6] += c.z; acc[7] += c.w;
+      }
+      float bb[8];
+      load8(p.bias + e, bb);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = bf16_round(acc[i] + bb[i]);
+    } else if (cached_row && p.cache_in != nullptr) {
+      load8(p.cache_in + size_t(row) * p.dim + e, o);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = 0.f;
+    }
+    if (cached_row && p.cache_out != nullptr) store8(p.cache_out + size_t(row) * p.dim + e, o);
+    float g[8], y[8], x[8];
+    modulation8(p.mod, p.time, p.ts, row, 5, p.dim, e, g);
+    load8(p.y + size_t(row) * p.dim + e, y);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      x[i] = bf16_round(y[i] + bf16_round(g[i] * o[i]));
+      xrow[e + i] = x[i];
+      local += x[i];
+    }
+    if (last) store8(p.x_final + size_t(row) * p.dim + e, x);
+    else store8(p.y + size_t(row) * p.dim + e, x);
+  }
+  if (last) {
+    if (tid == 0) pdl_launch_dependents();
+    return;
+  }
+  __syncthreads();
+  if (p.next_pos != nullptr && tid == 0) p.next_pos[row] = last_match;
+
+  // 2. Layer l+1: LayerNorm + adaLN (FFN shift/scale slots 3 and 4), gather.
+  const float mean = block_sum(local, red) / float(p.dim);
+  local = 0.f;
+  for (int v = tid; v < nvec; v += blockDim.x) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float c = xrow[v * 8 + i] - mean;
+      local += c * c;
+    }
+  }
+  const float var = block_sum(local, red) / float(p.dim);
+  const float rstd = rsqrtf(var + p.eps);
+  const int nm = n_match < kMaxMatches ? n_match : kMaxMatches;
+  for (int v = tid; v < nvec; v += blockDim.x) {
+    const int e = v * 8;
+    float n[8], shift[8], scale[8];
+    modulation8(p.next_mod, p.time, p.ts, row, 3, p.dim, e, shift);
+    modulation8(p.next_mod, p.time, p.ts, row, 4, p.dim, e, scale);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float s1 = bf16_round(1.0f + scale[i]);
+      n[i] = bf16_round(bf16_round((xrow[e + i] - mean) * rstd) * s1) + shift[i];
+    }
+    for (int k = 0; k < nm; ++k) store8(p.next_gathered + size_t(matches[k]) * p.dim + e, n);
+  }
+  if (tid == 0) pdl_launch_dependents();
+}
+
 // Weight repack: dst[n/128][k/64][128][64] <- src[n][k] (16-byte vectors;
 // stores are contiguous, each group of 8 threads reads 128 contiguous bytes).
 __global__ void pack_weight_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int n_out, int k_in) {

@@ -12,10 +12,11 @@ Transformer runs at Euler updates 0 and 3 only, so the FFN stack runs twice.
   (``WAMInfer/blocks.py:249-264``, ``WAMInfer/runtime.py:263``).
 * update 3 (full refresh): every row of every layer.
 
-Each layer is one ``wamffn_block_run`` (norm + gather, up GEMM, down GEMM,
-reduce + scatter + gated residual); layers chain through ping-pong residual
-buffers.  Everything a request touches is preallocated, so a request (or a
-batch of them) can be captured into one CUDA graph.
+A pass is one ``wamffn_stack_run``: up GEMM, down GEMM and one fused
+layer-boundary kernel per layer (split-K reduction, history scatter, gated
+residual, next layer's norm + gather).  Everything a request touches is
+preallocated, so a request (or a batch of them) can be captured into one
+CUDA graph.
 """
 
 from __future__ import annotations
@@ -119,6 +120,10 @@ class FFNStack:
         self.plan = BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d, d_hidden=geo.h)
         self._pingpong = [torch.empty(geo.seq, geo.d, device=device, dtype=torch.bfloat16) for _ in range(2)]
         self._keep = []  # argument structs referenced by enqueued launches
+        self._layer_array = (_lib.LayerWeights * len(weights))()
+        for i, (w, (w_up, w_down)) in enumerate(zip(weights, self.packed)):
+            self._layer_array[i] = _lib.LayerWeights(w_up.data_ptr(), w.b_up.data_ptr(), w_down.data_ptr(),
+                                                     w.b_down.data_ptr(), w.mod.data_ptr())
 
     def _args(self, layer: int, x, x_out, time, indices=None, cache_in=None, cache_out=None, n=0):
         w = self.weights[layer]
@@ -146,8 +151,34 @@ class FFNStack:
         return a
 
     def enqueue_pass(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
-        """Runs the L layers; with `reuse`, layers 1.. gather its indices and
-        update its history."""
+        """Runs the L layers with one ``wamffn_stack_run`` (fused layer
+        boundaries); with `reuse`, layers 1.. gather its indices and read /
+        write its history."""
+        geo = self.geo
+        a = _lib.StackArgs()
+        a.layers = len(self.weights)
+        a.weights = ctypes.cast(self._layer_array, ctypes.POINTER(_lib.LayerWeights))
+        a.weights_packed = 1
+        a.x = x_in.data_ptr()
+        a.time = time.data_ptr()
+        a.time_stride = 6 * geo.d
+        a.seq = geo.seq
+        if reuse is not None:
+            a.indices = reuse.indices.data_ptr()
+            a.index_bytes = reuse.indices.element_size()
+            a.rows = reuse.indices.numel()
+            a.first_gathered_layer = 1
+            a.cache_rows = geo.current
+            a.cache_in = reuse.history_in.data_ptr()
+            a.cache_out = reuse.history_out.data_ptr()
+        a.x_out = x_final.data_ptr()
+        a.eps = self.eps
+        self._keep.append(a)
+        _lib.check(_lib.lib().wamffn_stack_run(self.plan.handle, stream, ctypes.byref(a)))
+
+    def enqueue_pass_blocks(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
+        """Same pass as ``enqueue_pass`` with one ``wamffn_block_run`` per layer
+        (four kernels per layer, no fused boundary)."""
         geo = self.geo
         src = x_in
         for layer in range(len(self.weights)):
@@ -167,7 +198,7 @@ class FFNStack:
         self.enqueue_pass(req.x[1], req.out[1], req.time[1], stream)              # update 3, full refresh
 
     def launches_per_request(self) -> int:
-        return 4 * 2 * self.geo.layers
+        return 2 * (1 + 3 * self.geo.layers)
 
     def close(self):
         self.plan.close()
