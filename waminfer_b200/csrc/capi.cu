@@ -128,6 +128,8 @@ int prepare_device(int device, int* sm_count) {
 struct GemmConfig {
   int rows = 0, n_out = 0, k_in = 0;
   int group = 1;  // CTAs per UMMA (2 = cta_group::2 pair)
+  int groups = 1;      // token groups (grid.z)
+  int group_rows = 0;  // rows per token group
   int tok_pad = 0, mma_n0 = 0, mma_n1 = 0, tok_box = 0, n_boxes = 0, b_rows = 0;
   int a_stages = 0, b_stages = 0, splits = 1;
   uint32_t tmem_cols = 0;
@@ -139,14 +141,21 @@ bool pair_enabled() {
   return on;
 }
 
-int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c) {
-  if (rows < 1 || rows > kMaxTokens)
-    return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d outside [1, %d]", rows, kMaxTokens);
+int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, int groups = 1) {
+  if (rows < 1 || rows > kMaxTokens * 4)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d outside [1, %d]", rows, kMaxTokens * 4);
+  if (groups < 1 || groups > 4) return fail(WAMFFN_ERR_UNSUPPORTED, "token groups=%d outside [1, 4]", groups);
+  const int total_rows = rows;
+  rows = (rows + groups - 1) / groups;  // rows per token group
+  if (rows > kMaxTokens)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "rows per token group=%d above %d", rows, kMaxTokens);
   if (n_out < kFeatTile || n_out % kFeatTile)
     return fail(WAMFFN_ERR_UNSUPPORTED, "n_out=%d must be a positive multiple of %d", n_out, kFeatTile);
   if (k_in < kBlockK || k_in % kBlockK)
     return fail(WAMFFN_ERR_UNSUPPORTED, "k_in=%d must be a positive multiple of %d", k_in, kBlockK);
-  c->rows = rows;
+  c->rows = total_rows;
+  c->groups = groups;
+  c->group_rows = rows;
   c->n_out = n_out;
   c->k_in = k_in;
   c->group = (pair_enabled() && (n_out / kFeatTile) % 2 == 0) ? 2 : 1;
@@ -228,6 +237,7 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   if (rc) return rc;
   GemmParams p{};
   p.tokens = c.rows;
+  p.group_rows = c.group_rows;
   p.tok_pad = c.tok_pad;
   p.mma_n0 = c.mma_n0;
   p.mma_n1 = c.mma_n1;
@@ -247,7 +257,7 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   p.status = status;
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned(c.n_out / kFeatTile), unsigned(c.splits), 1);
+  cfg.gridDim = dim3(unsigned(c.n_out / kFeatTile), unsigned(c.splits), unsigned(c.groups));
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = size_t(c.smem_bytes);
   cfg.stream = stream;
@@ -257,7 +267,7 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   attr[1].id = cudaLaunchAttributeClusterDimension;
   attr[1].val.clusterDim.x = unsigned(c.group);
   attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
+  attr[1].val.clusterDim.z = 1;  // token groups are independent: clusters of more than 2 CTAs fit fewer SMs
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   if (c.group == 2) WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<2>, tm_w, tm_x, p));
@@ -633,13 +643,31 @@ int wamffn_block_plan_destroy(wamffn_block_plan* plan) {
 }
 
 namespace {
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
+
 int block_configs(const wamffn_block_plan* plan, int rows, GemmConfig* up, GemmConfig* down) {
   int rc = make_gemm_config(rows, plan->h, plan->d, default_splits(plan->h, plan->d, plan->sm_count), up);
   if (rc) return rc;
+  // Down projection: K = h is long and the output narrow, so the SMs are filled
+  // with split-K (optionally x token groups).
+  // Token groups (grid.z) halve the partials but made the mainloop HBM-bound
+  // (the groups re-stream each weight tile): one group unless overridden.
+  static const int groups_env = env_int("WAMFFN_DOWN_GROUPS", 0);
+  int groups = groups_env > 0 ? groups_env : 1;
+  const int tiles = plan->d / kFeatTile;
   int s = plan->split_override[rows];
-  if (s <= 0) s = default_splits(plan->d, plan->h, plan->sm_count);
+  if (s <= 0) {
+    s = 1;
+    for (int c = 2; c <= 16; ++c) {
+      if (tiles * c * groups > plan->sm_count || (plan->h / kBlockK) / c < 8) break;
+      s = c;
+    }
+  }
   if (s > plan->max_splits) s = plan->max_splits;
-  return make_gemm_config(rows, plan->d, plan->h, s, down);
+  return make_gemm_config(rows, plan->d, plan->h, s, down, groups);
 }
 }  // namespace
 
@@ -809,7 +837,8 @@ int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_
     b.dim = d;
     b.seq = a->seq;
     b.bias = static_cast<const __nv_bfloat16*>(w.b_down);
-    b.pos = gathered_layer(l) ? plan->pos : nullptr;
+    b.idx = gathered_layer(l) ? a->indices : nullptr;
+    b.idx_bytes = a->index_bytes;
     if (gathered_layer(l)) {
       const size_t slot = size_t(l - a->first_gathered_layer) * layer_cache;
       b.cache_rows = a->cache_rows;
@@ -826,7 +855,6 @@ int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_
     b.next_idx_bytes = a->index_bytes;
     b.next_m = last ? 0 : layer_rows(l + 1);
     b.next_gathered = plan->gathered;
-    b.next_pos = plan->pos;
     b.x_final = static_cast<__nv_bfloat16*>(a->x_out);
     b.eps = a->eps;
     b.status = plan->status;

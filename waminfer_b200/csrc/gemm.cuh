@@ -33,7 +33,9 @@
 //   warp 3      idle
 //   epilogue    all 12 warps once their roles are done: warp w reads TMEM
 //               lanes 32*(w%4).. and every third 32-column chunk
-// Grid: (n_total / 128, split_k), clusters of (kGroup, 1, 1).  With
+// Grid: (n_total / 128, split_k, token groups), clusters of (kGroup, 1,
+// token groups): the token groups of one weight tile sit in one cluster, so
+// they stream the same weight tiles side by side and share them in L2.  With
 // split_k > 1 each CTA covers a contiguous range of K blocks and writes an
 // fp32 partial; a row kernel sums the partials in split order
 // (deterministic, no atomics).
@@ -57,7 +59,8 @@ constexpr int kSmemLimit = 232448;     // 227 KB opt-in dynamic shared memory
 constexpr int kSmemReserve = 1024 + 512;  // alignment slack + barriers
 
 struct GemmParams {
-  int tokens;        // real activation rows
+  int tokens;        // real activation rows (all token groups)
+  int group_rows;    // rows per token group (grid.z); == tokens with one group
   int tok_pad;       // tokens rounded up to the MMA granularity
   int mma_n0;        // N of the first UMMA (<= 256, multiple of 16)
   int mma_n1;        // N of the second UMMA (0 when one suffices)
@@ -83,6 +86,7 @@ __host__ __device__ constexpr int gemm_a_bytes() { return kFeatTile * kBlockK * 
 // record = {tag, start, operands ready, MMAs issued, accumulator ready,
 // epilogue done, sm id, k blocks}; globaltimer nanoseconds.
 constexpr int kTraceWords = 8;
+constexpr unsigned int kTraceBoundary = 7;  // record tag of the layer-boundary kernel
 __device__ unsigned long long* g_trace = nullptr;
 __device__ unsigned int g_trace_capacity = 0;
 
@@ -101,8 +105,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Clusters are (kGroup, 1, token groups): CTAs 2k and 2k+1 form a UMMA pair.
   const uint32_t rank = kGroup == 2 ? cluster_ctarank() : 0u;
-  const bool leader = rank == 0;
+  const uint32_t pair_rank = rank & 1u;
+  const uint32_t leader_rank = rank & ~1u;
+  const bool leader = pair_rank == 0;
+  const uint16_t pair_mask = uint16_t(0x3u << leader_rank);
+  // This CTA's token group.
+  const int tok_base = blockIdx.z * p.group_rows;
+  const int tokens = min(p.group_rows, p.tokens - tok_base);
 
   const int a_bytes = gemm_a_bytes();
   const int b_bytes = p.b_rows * kBlockK * 2;
@@ -187,7 +198,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (elect_one()) {
         const uint32_t local_full = smem_addr(&full[s]);
         // The leader's barrier counts both CTAs' bytes; the peer only adds its copies.
-        const uint32_t fb = kGroup == 2 ? map_to_cta(local_full, 0) : local_full;
+        const uint32_t fb = kGroup == 2 ? map_to_cta(local_full, leader_rank) : local_full;
         if (leader) mbar_arrive_expect_tx(local_full, uint32_t(bytes * kGroup));
         const int kx = (kb0 + i) * kBlockK;
         if (weights) {
@@ -201,9 +212,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t dst = smem_addr(ring + s * bytes + b * p.tok_box * kBlockK * 2);
             if constexpr (kGroup == 2) {
               // Box b feeds UMMA b: this CTA holds its rank's half of that UMMA's tokens.
-              tma_load_2d_pair(dst, &tm_x, fb, kx, b * (2 * p.tok_box) + int(rank) * p.tok_box, policy);
+              tma_load_2d_pair(dst, &tm_x, fb, kx, tok_base + b * (2 * p.tok_box) + int(pair_rank) * p.tok_box,
+                               policy);
             } else {
-              tma_load_2d(dst, &tm_x, fb, kx, b * p.tok_box, policy);
+              tma_load_2d(dst, &tm_x, fb, kx, tok_base + b * p.tok_box, policy);
             }
           }
         }
@@ -267,8 +279,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           // Free both stages (in both CTAs) once these MMAs have read them.
           if constexpr (kGroup == 2) {
-            umma_commit_pair(smem_addr(&empty_a[sa]), 0x3);
-            umma_commit_pair(smem_addr(&empty_b[sb]), 0x3);
+            umma_commit_pair(smem_addr(&empty_a[sa]), pair_mask);
+            umma_commit_pair(smem_addr(&empty_b[sb]), pair_mask);
           } else {
             umma_commit(smem_addr(&empty_a[sa]));
             umma_commit(smem_addr(&empty_b[sb]));
@@ -278,7 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       // Accumulator complete (or pipeline aborted): release the epilogues.
       if (elect_one()) {
-        if constexpr (kGroup == 2) umma_commit_pair(smem_addr(tmem_full), 0x3);
+        if constexpr (kGroup == 2) umma_commit_pair(smem_addr(tmem_full), pair_mask);
         else umma_commit(smem_addr(tmem_full));
       }
       __syncwarp();
@@ -308,20 +320,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (rec) rec[4] = globaltimer_ns();
     if (ok) {
       const int f = n0 + q * 32 + lane;
-      const int nchunks = (p.tokens + 31) >> 5;
+      const int nchunks = (tokens + 31) >> 5;
       const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
       if (p.epi == EPI_PARTIAL_F32) {
         // Partials are re-read once by the split-K reduction: keep them in L2.
         const uint64_t keep = l2_policy_evict_last();
-        float* out = reinterpret_cast<float*>(p.out) + size_t(split) * p.tokens * p.n_total + f;
+        float* out = reinterpret_cast<float*>(p.out) + (size_t(split) * p.tokens + tok_base) * p.n_total + f;
         for (int c = group; c < nchunks; c += 3) {
           uint32_t r[32];
           tmem_ld32(lane_addr + uint32_t(c * 32), r);
-          tmem_wait_ld();
+          tmem_wait_ld(r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int t = c * 32 + i;
-            if (t < p.tokens) st_global_keep(out + size_t(t) * p.n_total, __uint_as_float(r[i]), keep);
+            if (t < tokens) st_global_keep(out + size_t(t) * p.n_total, __uint_as_float(r[i]), keep);
           }
         }
       } else {
@@ -335,11 +347,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int n_base = n0 + q * 32;
         // 16-column chunks: the GELU math keeps 16 values in flight per thread
         // (32 measured slower: the longer dependency chains do not overlap).
-        const int nchunks16 = (p.tokens + 15) >> 4;
+        const int nchunks16 = (tokens + 15) >> 4;
+        // Software pipeline: the TMEM load of the next chunk is in flight
+        // while this chunk's GELU runs.
+        uint32_t nxt[16];
+        if (group < nchunks16) tmem_ld16(lane_addr + uint32_t(group * 16), nxt);
         for (int c = group; c < nchunks16; c += 3) {
+          tmem_wait_ld(nxt);
           uint32_t r[16];
-          tmem_ld16(lane_addr + uint32_t(c * 16), r);
-          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) r[i] = nxt[i];
+          if (c + 3 < nchunks16) tmem_ld16(lane_addr + uint32_t((c + 3) * 16), nxt);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             float v = __uint_as_float(r[i]) + bias;
@@ -353,7 +371,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const int col = (lane & 3) * 8;
             const int t = c * 16 + row;
             const uint4 v = *reinterpret_cast<const uint4*>(&tile[row * 32 + col]);
-            if (t < p.tokens) *reinterpret_cast<uint4*>(&out[size_t(t) * p.n_total + n_base + col]) = v;
+            if (t < tokens) *reinterpret_cast<uint4*>(&out[size_t(tok_base + t) * p.n_total + n_base + col]) = v;
           }
           __syncwarp();
         }

@@ -97,6 +97,28 @@ __device__ __forceinline__ void modulation8(const __nv_bfloat16* mod, const __nv
   for (int i = 0; i < 8; ++i) out[i] = bf16_round(a[i] + b[i]);
 }
 
+__device__ __forceinline__ void unpack8(const uint4 u, float (&v)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// modulation8 kept packed (the values are bf16 by construction): 4 registers.
+__device__ __forceinline__ uint4 modulation8_packed(const __nv_bfloat16* mod, const __nv_bfloat16* time,
+                                                    long long ts, int row, int slot, int dim, int e) {
+  float v[8];
+  modulation8(mod, time, ts, row, slot, dim, e, v);
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return u;
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -127,6 +149,9 @@ __global__ void __launch_bounds__(kRowThreads) modnorm_kernel(const NormParams p
   const int nvec = p.dim >> 3;
 
   if (p.pdl) pdl_wait_prior();
+  // Let the next kernel (the GEMM) be scheduled as SMs free up; it still waits
+  // for this grid's completion before reading what it writes.
+  if (tid == 0) pdl_launch_dependents();
 
   // Pad / invalid gather entries: the activation row is zero so the GEMM
   // computes on defined data; invalid ones also raise the status bit.
@@ -258,6 +283,7 @@ __global__ void __launch_bounds__(kRowThreads) rowepi_kernel(const EpiParams p) 
   const int tid = threadIdx.x;
   const int nvec = p.dim >> 3;
   if (p.pdl) pdl_wait_prior();
+  if (tid == 0) pdl_launch_dependents();
   int j = p.pos_of_row != nullptr ? p.pos_of_row[row] : row;
   if (j >= p.m) j = -1;
   const bool cached_row = row < p.cache_rows;
@@ -314,7 +340,8 @@ struct BoundaryParams {
   int dim;
   int seq;
   const __nv_bfloat16* bias;    // b_down of layer l
-  const int* pos;               // [seq] gather position of layer l, or null (identity)
+  const void* idx;              // gather list of layer l ([m] entries), or null (identity)
+  int idx_bytes;
   int cache_rows;
   const __nv_bfloat16* cache_in;
   __nv_bfloat16* cache_out;
@@ -327,48 +354,74 @@ struct BoundaryParams {
   int next_idx_bytes;
   int next_m;
   __nv_bfloat16* next_gathered; // [next_m, dim]
-  int* next_pos;                // [seq]
   __nv_bfloat16* x_final;       // [seq, dim], written after the last layer
   float eps;
   unsigned int* status;
 };
 
+constexpr int kBoundarySplitsBatch = 2;  // split-K partials loaded per batch of independent loads
+
 // Dynamic shared memory: dim floats.
-__global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryParams p) {
+//
+// The gather lists do not depend on the down projection and are read before
+// the grid-dependency wait; after it the residual row, the gate, the bias and
+// the partials are read in batches of independent loads.  Registers are capped so that three CTAs (three rows)
+// stay resident per SM.
+__global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const BoundaryParams p) {
   extern __shared__ float xrow[];
   __shared__ float red[32];
   __shared__ int matches[kMaxMatches];
   __shared__ int n_match;
-  __shared__ int last_match;
+  __shared__ int last_match;   // this layer: last j with idx[j] == row, -1 if none
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   const int nvec = p.dim >> 3;
-  pdl_wait_prior();
-
   const bool last = p.next_mod == nullptr;
+
   if (!last && p.next_idx != nullptr && b < p.next_m) {
     const long long r = load_index(p.next_idx, p.next_idx_bytes, b);
     if (r < 0 || r >= p.seq) {
       if (r != -1 && tid == 0) atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+      // The activation buffer is read by the running down projection: zero
+      // the slot only after it has finished.
+      pdl_wait_prior();
       for (int v = tid; v < nvec; v += blockDim.x)
         *reinterpret_cast<uint4*>(p.next_gathered + size_t(b) * p.dim + v * 8) = make_uint4(0, 0, 0, 0);
     }
   }
-  if (b >= p.seq) return;
+  if (b >= p.seq) {
+    pdl_wait_prior();
+    if (tid == 0) pdl_launch_dependents();
+    return;
+  }
   const int row = b;
+  unsigned long long* rec = nullptr;  // optional timeline record (wamffn_trace_enable)
+  if (g_trace != nullptr && tid == 0) {
+    const unsigned int slot = atomicAdd(reinterpret_cast<unsigned int*>(g_trace), 1u);
+    if (slot + 1 < g_trace_capacity) {
+      rec = g_trace + size_t(slot + 1) * kTraceWords;
+      rec[0] = (unsigned long long)b | (unsigned long long)kTraceBoundary << 32;
+      rec[1] = globaltimer_ns();
+      rec[6] = smid();
+    }
+  }
 
-  // Gather slots of the next layer that read this row.
+  // Which entry of this layer's list computed this row, and which entries of
+  // the next layer's list read it (both lists are inputs of the whole pass).
   if (tid == 0) {
     n_match = 0;
-    last_match = -1;
+    last_match = p.idx == nullptr ? (row < p.m ? row : -1) : -1;
   }
   __syncthreads();
+  if (p.idx != nullptr) {
+    for (int j = tid; j < p.m; j += blockDim.x)
+      if (load_index(p.idx, p.idx_bytes, j) == row) atomicMax(&last_match, j);
+  }
   if (!last) {
     if (p.next_idx == nullptr) {
       if (tid == 0 && row < p.next_m) {
         matches[0] = row;
         n_match = 1;
-        last_match = row;
       }
     } else {
       for (int j = tid; j < p.next_m; j += blockDim.x) {
@@ -376,30 +429,49 @@ __global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryPar
           const int slot = atomicAdd(&n_match, 1);
           if (slot < kMaxMatches) matches[slot] = j;
           else atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
-          atomicMax(&last_match, j);
         }
       }
     }
   }
-
-  // 1. Layer l: reduce, bias, scatter into the history, gated residual.
-  int j = p.pos != nullptr ? p.pos[row] : row;
-  if (j >= p.m) j = -1;
+  __syncthreads();
+  const int j = last_match;
   const bool cached_row = row < p.cache_rows;
   if (j < 0 && !cached_row && tid == 0) atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
+
+  pdl_wait_prior();
+  if (tid == 0) pdl_launch_dependents();
+  if (rec) rec[2] = globaltimer_ns();
+
+  // 1. Layer l: reduce, bias, scatter into the history, gated residual.
   float local = 0.f;
   for (int v = tid; v < nvec; v += blockDim.x) {
     const int e = v * 8;
+    const uint4 y_packed = *reinterpret_cast<const uint4*>(p.y + size_t(row) * p.dim + e);
+    const uint4 g_packed = modulation8_packed(p.mod, p.time, p.ts, row, 5, p.dim, e);
     float o[8];
     if (j >= 0) {
+      const float* base = p.partial + size_t(j) * p.dim + e;
+      const size_t split_stride = size_t(p.m) * p.dim;
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int s = 0; s < p.splits; ++s) {
-        const float4* src = reinterpret_cast<const float4*>(p.partial + (size_t(s) * p.m + j) * p.dim + e);
-        const float4 a = src[0], c = src[1];
-        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-        acc[4] += c.x; acc[5] += c.y; acc[6] += c.z; acc[7] += c.w;
+      for (int s0 = 0; s0 < p.splits; s0 += kBoundarySplitsBatch) {
+        float4 part[kBoundarySplitsBatch][2];
+#pragma unroll
+        for (int s = 0; s < kBoundarySplitsBatch; ++s) {
+          if (s0 + s < p.splits) {
+            const float4* src = reinterpret_cast<const float4*>(base + (s0 + s) * split_stride);
+            part[s][0] = src[0];
+            part[s][1] = src[1];
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < kBoundarySplitsBatch; ++s) {
+          if (s0 + s < p.splits) {
+            acc[0] += part[s][0].x; acc[1] += part[s][0].y; acc[2] += part[s][0].z; acc[3] += part[s][0].w;
+            acc[4] += part[s][1].x; acc[5] += part[s][1].y; acc[6] += part[s][1].z; acc[7] += part[s][1].w;
+          }
+        }
       }
       float bb[8];
       load8(p.bias + e, bb);
@@ -412,9 +484,9 @@ __global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryPar
       for (int i = 0; i < 8; ++i) o[i] = 0.f;
     }
     if (cached_row && p.cache_out != nullptr) store8(p.cache_out + size_t(row) * p.dim + e, o);
-    float g[8], y[8], x[8];
-    modulation8(p.mod, p.time, p.ts, row, 5, p.dim, e, g);
-    load8(p.y + size_t(row) * p.dim + e, y);
+    float g[8], x[8], y[8];
+    unpack8(g_packed, g);
+    unpack8(y_packed, y);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       x[i] = bf16_round(y[i] + bf16_round(g[i] * o[i]));
@@ -424,14 +496,19 @@ __global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryPar
     if (last) store8(p.x_final + size_t(row) * p.dim + e, x);
     else store8(p.y + size_t(row) * p.dim + e, x);
   }
+  if (rec) rec[3] = rec[4] = globaltimer_ns();
   if (last) {
-    if (tid == 0) pdl_launch_dependents();
+    if (rec) rec[5] = globaltimer_ns();
     return;
   }
-  __syncthreads();
-  if (p.next_pos != nullptr && tid == 0) p.next_pos[row] = last_match;
 
   // 2. Layer l+1: LayerNorm + adaLN (FFN shift/scale slots 3 and 4), gather.
+  // The first vector's shift / scale loads overlap the two reductions.
+  uint4 pre_shift = make_uint4(0, 0, 0, 0), pre_scale = make_uint4(0, 0, 0, 0);
+  if (tid < nvec) {
+    pre_shift = modulation8_packed(p.next_mod, p.time, p.ts, row, 3, p.dim, tid * 8);
+    pre_scale = modulation8_packed(p.next_mod, p.time, p.ts, row, 4, p.dim, tid * 8);
+  }
   const float mean = block_sum(local, red) / float(p.dim);
   local = 0.f;
   for (int v = tid; v < nvec; v += blockDim.x) {
@@ -447,8 +524,13 @@ __global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryPar
   for (int v = tid; v < nvec; v += blockDim.x) {
     const int e = v * 8;
     float n[8], shift[8], scale[8];
-    modulation8(p.next_mod, p.time, p.ts, row, 3, p.dim, e, shift);
-    modulation8(p.next_mod, p.time, p.ts, row, 4, p.dim, e, scale);
+    if (v == tid) {
+      unpack8(pre_shift, shift);
+      unpack8(pre_scale, scale);
+    } else {
+      modulation8(p.next_mod, p.time, p.ts, row, 3, p.dim, e, shift);
+      modulation8(p.next_mod, p.time, p.ts, row, 4, p.dim, e, scale);
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float s1 = bf16_round(1.0f + scale[i]);
@@ -456,7 +538,7 @@ __global__ void __launch_bounds__(kRowThreads) boundary_kernel(const BoundaryPar
     }
     for (int k = 0; k < nm; ++k) store8(p.next_gathered + size_t(matches[k]) * p.dim + e, n);
   }
-  if (tid == 0) pdl_launch_dependents();
+  if (rec) rec[5] = globaltimer_ns();
 }
 
 // Weight repack: dst[n/128][k/64][128][64] <- src[n][k] (16-byte vectors;
