@@ -73,6 +73,21 @@ def test_up_projection_gelu(cuda_device, weights, packed, rows, layout):
     plan.close()
 
 
+@pytest.mark.parametrize("rows", [16, 128])
+def test_tuned_gelu_plan_never_splits_k(cuda_device, weights, packed, rows):
+    """The split-K reduction applies the bias only, so tuning must keep GELU
+    plans at one split (the tuner times the candidates on the device)."""
+    from waminfer_b200.ffn import Plan
+
+    x = randn((rows, D), cuda_device, weights["gen"])
+    plan = Plan(x, packed["w_up"], weights["b_up"], exhaustive=True, gelu=True)
+    assert plan.selected_configuration()[4] == 1
+    out = plan.run(x, packed["w_up"], weights["b_up"])
+    ref = offn.bf16(offn.gelu_tanh(x.float() @ weights["w_up"].float().T + weights["b_up"].float()))
+    close(out, ref)
+    plan.close()
+
+
 @pytest.mark.parametrize("layout", ["packed", "rowmajor"])
 @pytest.mark.parametrize("rows", [1, 17, 240, 272, 304, 360, 392, 512])
 def test_down_projection_split_k(cuda_device, weights, packed, rows, layout):

@@ -435,7 +435,9 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
   plan->device = device;
   plan->gelu = (flags & WAMFFN_LINEAR_GELU) ? 1 : 0;
   plan->packed = (flags & WAMFFN_WEIGHTS_PACKED) ? 1 : 0;
-  rc = make_gemm_config(rows, n_out, k_in, default_splits(n_out, k_in, sm), &plan->cfg);
+  // GELU is applied in the GEMM epilogue, so a GELU plan never splits K (the
+  // split-K reduction applies the bias only).
+  rc = make_gemm_config(rows, n_out, k_in, plan->gelu ? 1 : default_splits(n_out, k_in, sm), &plan->cfg);
   if (rc) {
     delete plan;
     return rc;
@@ -454,7 +456,7 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
     // Candidate split-K factors are timed on scratch operands, the way the
     // reference times every candidate algorithm (cpp:121-158).
     int max_s = 1;
-    for (int s = 2; s <= 16 && tiles * s <= 2 * sm && (k_in / kBlockK) / s >= 4; ++s) max_s = s;
+    for (int s = 2; !plan->gelu && s <= 16 && tiles * s <= 2 * sm && (k_in / kBlockK) / s >= 4; ++s) max_s = s;
     void *x = nullptr, *w = nullptr, *b = nullptr, *o = nullptr;
     bool okalloc = cudaMalloc(&x, size_t(rows) * k_in * 2) == cudaSuccess &&
                    cudaMalloc(&w, size_t(n_out) * k_in * 2) == cudaSuccess &&
