@@ -115,6 +115,44 @@ int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values
  * Synchronises the device. */
 int wamffn_linear_status(wamffn_linear_plan* plan, uint32_t* status, int clear);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free split-K linear.  No counterpart in the reference: it exists
+ * for callers that must not allocate device memory at all -- code that runs
+ * inside an allocator or memory-pool callback (a cudaMalloc there would
+ * re-enter the allocator), plugin hosts that own every byte of device memory
+ * and forbid allocations by plugins, and serving processes that reserved all
+ * of HBM for their caches at start-up.  Such a caller cannot create a plan
+ * (plan creation allocates its workspace and status word).
+ *
+ * out[rows, n_out] = x[rows, k_in] . weight^T + bias, bf16 in and out, fp32
+ * accumulation, K split into `splits` (2..16) slices whose fp32 partials live
+ * in one static device array of WAMFFN_STATIC_SCRATCH_BYTES per device (the
+ * first 256 bytes hold a status word, the partials follow).  A call needs
+ * 256 + splits * rows * n_out * 4 bytes of it; a call that needs more is
+ * rejected with WAMFFN_ERR_INVALID before anything is launched.  flags accepts
+ * WAMFFN_WEIGHTS_PACKED only (there is no GELU variant: the split-K reduction
+ * applies the bias only).  Same shape limits as wamffn_linear_plan_create.
+ *
+ * The call allocates nothing: no cudaMalloc / cudaFree, no library routine
+ * that allocates.  The first call on a device looks up the array's address
+ * (cudaGetSymbolAddress with that device current, which may load the module
+ * on it) and sets the kernels' shared-memory limit: make that first call
+ * before any stream capture.  Later calls only encode tensor maps on the host
+ * and launch.
+ *
+ * Every call on a device shares the one array, so calls that overlap in time
+ * (two streams, or two host threads) race on it: serialise them.  Nothing in
+ * the array needs to start at zero except the status word, which each call
+ * clears on `stream` when `status` is null.  `status` may instead point at a
+ * caller-owned device word (4-byte aligned, cleared by the caller) that the
+ * kernels OR WAMFFN_DEV_* bits into; with null the bits land in the shared
+ * word and are not reported.
+ * ---------------------------------------------------------------------- */
+#define WAMFFN_STATIC_SCRATCH_BYTES (16u << 20) /* 16 MiB per device */
+int wamffn_linear_run_static(int device, void* stream, int rows, int n_out, int k_in, int splits,
+                             int flags, const void* x, const void* weight, const void* bias, void* out,
+                             uint32_t* status);
+
 /* PreparedFFN.forward (ffn.py:96-107): out = down(gelu(up(x))).  `up` and
  * `down` are plans of matching rows; hidden is scratch owned by the up plan. */
 int wamffn_ffn_run(wamffn_linear_plan* up, wamffn_linear_plan* down, void* stream, const void* x,

@@ -18,6 +18,11 @@
 #include "select.cuh"
 #include "wamffn.h"
 
+// Scratch of wamffn_linear_run_static, one copy per device shared by every
+// call: a status word in the first 256 bytes, then [splits, rows, n_out] fp32
+// split-K partials.
+static __device__ __align__(256) unsigned char g_static_scratch[WAMFFN_STATIC_SCRATCH_BYTES];
+
 using namespace wamffn;
 
 namespace {
@@ -536,6 +541,92 @@ int wamffn_linear_status(wamffn_linear_plan* plan, uint32_t* status, int clear) 
   WAMFFN_CUDA(cudaMemcpy(status, plan->status, sizeof(uint32_t), cudaMemcpyDeviceToHost));
   if (clear) WAMFFN_CUDA(cudaMemset(plan->status, 0, sizeof(uint32_t)));
   return WAMFFN_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+constexpr size_t kStaticScratchHeader = 256;  // status word, padded to the array's alignment
+std::mutex g_static_mu;
+void* g_static_base[64] = {};
+
+// Device address of g_static_scratch on `device` (which must be current),
+// looked up once per device.
+int static_scratch_base(int device, unsigned char** base) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_base[device] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess)
+      return fail(WAMFFN_ERR_CUDA, "cudaGetSymbolAddress of the static scratch on device %d: %s", device,
+                  cudaGetErrorString(e));
+    g_static_base[device] = ptr;
+  }
+  *base = static_cast<unsigned char*>(g_static_base[device]);
+  return WAMFFN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wamffn_linear_run_static(int device, void* stream_, int rows, int n_out, int k_in, int splits, int flags,
+                             const void* x, const void* weight, const void* bias, void* out, uint32_t* status) {
+  if (flags & ~WAMFFN_WEIGHTS_PACKED)
+    return fail(WAMFFN_ERR_INVALID,
+                "flags=%d: only WAMFFN_WEIGHTS_PACKED is accepted (the split-K reduction applies the bias only)",
+                flags);
+  if (splits < 2 || splits > 16) return fail(WAMFFN_ERR_INVALID, "splits=%d outside [2, 16]", splits);
+  if (device < 0 || device >= 64) return fail(WAMFFN_ERR_INVALID, "bad device %d", device);
+  if (!x || !weight || !bias || !out) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(bias) || !aligned16(out))
+    return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
+  if (status && (reinterpret_cast<uintptr_t>(status) & 3u))
+    return fail(WAMFFN_ERR_INVALID, "status must be 4-byte aligned");
+  GemmConfig c;
+  int rc = make_gemm_config(rows, n_out, k_in, splits, &c);
+  if (rc) return rc;
+  if (c.splits != splits)
+    return fail(WAMFFN_ERR_INVALID, "splits=%d exceeds the %d K blocks of k_in=%d", splits, k_in / kBlockK, k_in);
+  const size_t need = kStaticScratchHeader + size_t(splits) * size_t(rows) * size_t(n_out) * sizeof(float);
+  if (need > size_t(WAMFFN_STATIC_SCRATCH_BYTES))
+    return fail(WAMFFN_ERR_INVALID,
+                "splits=%d x rows=%d x n_out=%d fp32 partials need %zu bytes of scratch; the static scratch "
+                "holds %zu bytes (WAMFFN_STATIC_SCRATCH_BYTES)",
+                splits, rows, n_out, need, size_t(WAMFFN_STATIC_SCRATCH_BYTES));
+  int sm = 0;
+  rc = prepare_device(device, &sm);
+  if (rc) return rc;
+  DeviceGuard guard(device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", device);
+  unsigned char* base = nullptr;
+  rc = static_scratch_base(device, &base);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  unsigned int* st = reinterpret_cast<unsigned int*>(status);
+  if (st == nullptr) {
+    st = reinterpret_cast<unsigned int*>(base);
+    WAMFFN_CUDA(cudaMemsetAsync(st, 0, sizeof(unsigned int), stream));
+  }
+  float* partial = reinterpret_cast<float*>(base + kStaticScratchHeader);
+  const bool pdl = pdl_enabled();
+  // The GEMM overwrites every partial it covers, so the partials need no clearing.
+  rc = launch_gemm(c, EPI_PARTIAL_F32, stream, weight, (flags & WAMFFN_WEIGHTS_PACKED) != 0, x, nullptr, partial,
+                   st, pdl);
+  if (rc) return rc;
+  EpiParams e{};
+  e.partial = partial;
+  e.splits = c.splits;
+  e.m = c.rows;
+  e.dim = c.n_out;
+  e.bias = static_cast<const __nv_bfloat16*>(bias);
+  e.pos_of_row = nullptr;
+  e.seq = c.rows;
+  e.output = static_cast<__nv_bfloat16*>(out);
+  e.status = st;
+  e.pdl = 1;
+  return launch_epi(e, stream, pdl);
 }
 
 int wamffn_ffn_run(wamffn_linear_plan* up, wamffn_linear_plan* down, void* stream, const void* x,
