@@ -81,3 +81,42 @@ def test_stack_follows_oracle_with_reuse(cuda_device):
     ok, msg = offn.check_close(req.out[0], x, max_abs=6e-2)
     assert ok, f"stack output: {msg}"
     stack.close()
+
+
+def test_persistent_pass_kernel_equals_three_kernel_stack(cuda_device, tmp_path):
+    """The opt-in persistent pass kernel (WAMFFN_PASS=1, one launch per pass)
+    computes the same bits as the default three-kernel stack; the variable is
+    read once per process, so each variant runs in its own interpreter."""
+    import os
+    import subprocess
+    import sys
+
+    script = tmp_path / "stack_pass.py"
+    script.write_text(
+        "import sys, torch\n"
+        "from waminfer_b200 import _lib\n"
+        "from waminfer_b200.stack import FFNStack, Geometry, Request, make_weights\n"
+        "dev = torch.device('cuda', 0)\n"
+        "geo = Geometry(layers=3)\n"
+        "stack = FFNStack(make_weights(geo.layers, geo.d, geo.h, dev, seed=7), geo, dev)\n"
+        "req = Request(geo, dev, seed=8)\n"
+        "s = torch.cuda.current_stream(dev).cuda_stream\n"
+        "c0 = _lib.launch_count()\n"
+        "stack.enqueue_pass(req.x[0], req.out[0], req.time[0], s, reuse=req)\n"
+        "stack.enqueue_pass(req.x[1], req.out[1], req.time[1], s)\n"
+        "launches = _lib.launch_count() - c0\n"
+        "torch.cuda.synchronize()\n"
+        "assert stack.plan.status() == 0\n"
+        "torch.save({'out0': req.out[0].cpu(), 'out1': req.out[1].cpu(), 'hist': req.history_out.cpu(),\n"
+        "            'launches': launches}, sys.argv[1])\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    results = {}
+    for flag in ("0", "1"):
+        env = dict(os.environ, WAMFFN_PASS=flag, PYTHONPATH=root)
+        out = tmp_path / f"pass{flag}.pt"
+        subprocess.run([sys.executable, str(script), str(out)], check=True, env=env, cwd=root, timeout=600)
+        results[flag] = torch.load(out)
+    assert results["1"]["launches"] == 2          # one pass kernel per pass
+    assert results["0"]["launches"] == 2 * (1 + 3 * 3)
+    for key in ("out0", "out1", "hist"):
+        assert torch.equal(results["0"][key], results["1"][key]), key

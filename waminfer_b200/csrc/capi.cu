@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "gemm.cuh"
+#include "pass.cuh"
 #include "rowops.cuh"
 #include "select.cuh"
 #include "wamffn.h"
@@ -123,6 +124,10 @@ int prepare_device(int device, int* sm_count) {
                                      kSmemLimit));
     WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemLimit));
+    cudaFuncAttributes pass_attr{};
+    WAMFFN_CUDA(cudaFuncGetAttributes(&pass_attr, stack_pass_kernel));  // its static barriers count too
+    WAMFFN_CUDA(cudaFuncSetAttribute(stack_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemLimit - int(pass_attr.sharedSizeBytes)));
     d.ready = true;
   }
   *sm_count = d.sm_count;
@@ -351,6 +356,8 @@ struct wamffn_block_plan {
   int max_splits = 1;
   int* pos = nullptr;                 // [max_seq]
   unsigned int* status = nullptr;
+  unsigned int* pass_bars = nullptr;  // phase counters of the persistent pass kernel
+  int pass_ctas = 0;                  // co-resident CTAs of the pass kernel (0: unavailable)
   int split_override[kMaxTokens + 1];  // tuned split-K per row count (0 = heuristic)
 };
 
@@ -716,8 +723,29 @@ int wamffn_block_plan_create(int device, int max_rows, int max_seq, int d_model,
             cudaMalloc(&plan->partial, size_t(plan->max_splits) * max_rows * d_model * 4) == cudaSuccess &&
             cudaMalloc(&plan->pos, size_t(max_seq) * sizeof(int)) == cudaSuccess &&
             cudaMalloc(&plan->status, sizeof(unsigned int)) == cudaSuccess &&
-            cudaMemset(plan->status, 0, sizeof(unsigned int)) == cudaSuccess;
+            cudaMemset(plan->status, 0, sizeof(unsigned int)) == cudaSuccess &&
+            cudaMalloc(&plan->pass_bars, (3 * kPassMaxLayers + 1) * sizeof(unsigned int)) == cudaSuccess;
   if (!ok) return cleanup(fail(WAMFFN_ERR_CUDA, "block plan allocation failed"));
+  {
+    // The pass kernel's grid barriers need every CTA resident at once: one CTA
+    // per SM, in clusters of two.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(sm & ~1), 1, 1);
+    cfg.blockDim = dim3(kPassThreads, 1, 1);
+    cfg.dynamicSmemBytes = 200 * 1024;  // one CTA per SM, like every real pass launch
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, stack_pass_kernel, &cfg) == cudaSuccess)
+      plan->pass_ctas = 2 * clusters < (sm & ~1) ? 2 * clusters : (sm & ~1);
+    else
+      cudaGetLastError();
+  }
   *out_plan = plan;
   return WAMFFN_OK;
 }
@@ -731,6 +759,7 @@ int wamffn_block_plan_destroy(wamffn_block_plan* plan) {
   cudaFree(plan->partial);
   cudaFree(plan->pos);
   cudaFree(plan->status);
+  cudaFree(plan->pass_bars);
   delete plan;
   return WAMFFN_OK;
 }
@@ -855,6 +884,148 @@ int wamffn_block_run(wamffn_block_plan* plan, void* stream_, const wamffn_block_
   return launch_epi(e, stream, pdl);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Split-K of the pass kernel's down projection: the three-kernel stack's
+// choice (fill the SMs with tiles x splits, at least 8 K blocks per split),
+// capped by the CTA pairs.
+int pass_down_splits(const wamffn_block_plan* plan) {
+  const int d = plan->d, h = plan->h;
+  int splits = 1;
+  for (int s = 2; s <= plan->max_splits; ++s) {
+    if ((d / kFeatTile) * s > plan->sm_count || (d / 256) * s > plan->pass_ctas / 2 || (h / kBlockK) / s < 8) break;
+    splits = s;
+  }
+  return splits;
+}
+
+// The persistent pass kernel (opt-in, WAMFFN_PASS=1) covers the stack when
+// every layer's up items fit one per CTA pair (its GELU epilogue borrows the
+// idle activation ring) and the geometry is the pair kernel's.  It computes
+// the same bits as the three-kernel stack; on B200 it measured about 5 %
+// slower per 30-layer pass (its row phase runs on a third of the threads the
+// layer-boundary kernel gets), so the three-kernel stack is the default.
+bool pass_usable(const wamffn_block_plan* plan, const wamffn_stack_args* a, bool gather) {
+  static const bool on = env_flag("WAMFFN_PASS", false);
+  if (!on || plan->pass_ctas < 2 || a->layers > kPassMaxLayers) return false;
+  if (plan->d > kPassRowThreads * kPassRowVec * 8 || plan->d % 256 || plan->h % 256) return false;
+  if (!pair_enabled()) return false;
+  const int npairs = plan->pass_ctas / 2;
+  if (plan->h / 256 > npairs) return false;
+  const int row_limit = a->seq > a->rows ? a->seq : a->rows;
+  if (row_limit > kPassRowSlots * kPassRowGroups * plan->pass_ctas) return false;
+  return true;
+}
+
+int pass_class_config(int rows, const wamffn_block_plan* plan, PassClass* c) {
+  GemmConfig g;
+  int rc = make_gemm_config(rows, plan->h, plan->d, 1, &g);
+  if (rc) return rc;
+  if (g.group != 2) return fail(WAMFFN_ERR_UNSUPPORTED, "the pass kernel runs 2-SM UMMA pairs only");
+  c->rows = rows;
+  c->tok_pad = g.tok_pad;
+  c->mma_n0 = g.mma_n0;
+  c->mma_n1 = g.mma_n1;
+  c->tok_box = g.tok_box;
+  c->n_boxes = g.n_boxes;
+  c->b_rows = g.b_rows;
+  return WAMFFN_OK;
+}
+
+int launch_pass(wamffn_block_plan* plan, const wamffn_stack_args* a, bool gather, cudaStream_t stream) {
+  static PassParams p;  // ~14 KB: kept off the host stack; guarded by the mutex below
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  memset(&p, 0, sizeof(p));
+  const int d = plan->d, h = plan->h, L = a->layers;
+  p.layers = L;
+  p.d = d;
+  p.h = h;
+  p.seq = a->seq;
+  p.first_gathered = gather ? a->first_gathered_layer : L;
+  p.w_packed = a->weights_packed != 0;
+  int rc = pass_class_config(a->seq, plan, &p.cls[0]);
+  if (rc) return rc;
+  rc = pass_class_config(gather ? a->rows : a->seq, plan, &p.cls[1]);
+  if (rc) return rc;
+  p.up_tiles = h / 256;
+  p.down_tiles = d / 256;
+  const int splits = pass_down_splits(plan);
+  p.down_splits = splits;
+  // Shared memory: the same ring split as the GEMM kernel; the activation
+  // ring also hosts the 24 KB of GELU transpose tiles.
+  const int budget = kSmemLimit - kSmemReserve;
+  const int b_rows = p.cls[0].b_rows > p.cls[1].b_rows ? p.cls[0].b_rows : p.cls[1].b_rows;
+  p.b_stage_bytes = b_rows * kBlockK * 2;
+  p.b_stages = (budget / 2) / p.b_stage_bytes;
+  if (p.b_stages > kMaxBStages) p.b_stages = kMaxBStages;
+  if (p.b_stages < 2) p.b_stages = 2;
+  p.b_region_bytes = p.b_stages * p.b_stage_bytes;
+  if (p.b_region_bytes < kPassTransposeBytes) p.b_region_bytes = kPassTransposeBytes;
+  p.a_stages = (budget - p.b_region_bytes) / gemm_a_bytes();
+  if (p.a_stages > kMaxAStages) p.a_stages = kMaxAStages;
+  if (p.a_stages < 2) return fail(WAMFFN_ERR_UNSUPPORTED, "pass kernel: fewer than 2 weight stages");
+  const size_t smem = 1024 + size_t(p.a_stages) * gemm_a_bytes() + size_t(p.b_region_bytes);
+  if (smem + 1024 > size_t(kSmemLimit)) return fail(WAMFFN_ERR_UNSUPPORTED, "pass kernel: %zu bytes of shared memory", smem);
+  for (int l = 0; l < L; ++l) {
+    const wamffn_layer_weights& w = a->weights[l];
+    rc = p.w_packed ? encode_operand(&p.tm_w_up[l], w.w_up, kBlockK, uint64_t(h) * (d / kBlockK), kBlockK * 2, kFeatTile)
+                    : encode_operand(&p.tm_w_up[l], w.w_up, d, h, uint64_t(d) * 2, kFeatTile);
+    if (rc) return rc;
+    rc = p.w_packed ? encode_operand(&p.tm_w_down[l], w.w_down, kBlockK, uint64_t(d) * (h / kBlockK), kBlockK * 2,
+                                     kFeatTile)
+                    : encode_operand(&p.tm_w_down[l], w.w_down, h, d, uint64_t(h) * 2, kFeatTile);
+    if (rc) return rc;
+    p.b_up[l] = static_cast<const __nv_bfloat16*>(w.b_up);
+    p.b_down[l] = static_cast<const __nv_bfloat16*>(w.b_down);
+    p.mod[l] = static_cast<const __nv_bfloat16*>(w.mod);
+  }
+  for (int c = 0; c < 2; ++c) {
+    rc = encode_operand(&p.tm_act[c], plan->gathered, d, p.cls[c].rows, uint64_t(d) * 2, uint32_t(p.cls[c].tok_box));
+    if (rc) return rc;
+    rc = encode_operand(&p.tm_hid[c], plan->hidden, h, p.cls[c].rows, uint64_t(h) * 2, uint32_t(p.cls[c].tok_box));
+    if (rc) return rc;
+  }
+  p.x = static_cast<const __nv_bfloat16*>(a->x);
+  p.time = static_cast<const __nv_bfloat16*>(a->time);
+  p.ts = a->time_stride;
+  p.y = plan->y;
+  p.gathered = plan->gathered;
+  p.hidden = plan->hidden;
+  p.partial = plan->partial;
+  p.idx = gather ? a->indices : nullptr;
+  p.idx_bytes = a->index_bytes;
+  p.cache_rows = gather ? a->cache_rows : 0;
+  p.cache_in = static_cast<const __nv_bfloat16*>(a->cache_in);
+  p.cache_out = static_cast<__nv_bfloat16*>(a->cache_out);
+  p.x_out = static_cast<__nv_bfloat16*>(a->x_out);
+  p.eps = a->eps;
+  p.bars = plan->pass_bars;
+  p.status = plan->status;
+  WAMFFN_CUDA(cudaMemsetAsync(plan->pass_bars, 0, (3 * L + 1) * sizeof(unsigned int), stream));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(plan->pass_ctas), 1, 1);
+  cfg.blockDim = dim3(kPassThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, stack_pass_kernel, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_args* a) {
   if (!plan || !a || !a->weights) return fail(WAMFFN_ERR_INVALID, "null argument");
   if (a->layers < 1) return fail(WAMFFN_ERR_INVALID, "layers=%d", a->layers);
@@ -889,6 +1060,8 @@ int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_
   const size_t layer_cache = size_t(a->cache_rows) * d;
   auto gathered_layer = [&](int l) { return gather && l >= a->first_gathered_layer; };
   auto layer_rows = [&](int l) { return gathered_layer(l) ? a->rows : a->seq; };
+
+  if (pass_usable(plan, a, gather)) return launch_pass(plan, a, gather, stream);
 
   // Prologue of the first layer: y = x, norm + gather into the activation buffer.
   NormParams n{};
