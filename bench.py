@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-gpu-baselines", action="store_true")
+    p.add_argument("--tp", action="store_true",
+                   help="tensor-parallel mode: every request's FFN hidden dimension split across the --gpus ranks "
+                        "(one all-reduce per layer, strong scaling); not the default bench line")
     return p.parse_args()
 
 
@@ -469,12 +472,111 @@ def run_ours(args, world, rank, local):
     stack.close()
 
 
+def run_tp(args, world, rank, local):
+    """Tensor-parallel arm: the same requests on every rank, h split across
+    the ranks, one all-reduce per layer.  Whole-job TFLOP/s counts each
+    request's FLOPs once (strong scaling)."""
+    import torch.distributed as dist
+
+    from waminfer_b200.stack import Geometry, Request, make_weights
+    from waminfer_b200.tp import TPStack, slice_weights
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    geo = Geometry(layers=args.layers)
+    weights = make_weights(geo.layers, geo.d, geo.h, device, seed=0)
+    shards = slice_weights(weights, rank, world) if world > 1 else weights
+    del weights
+    if world > 1:
+        stack = TPStack(shards, geo, device)
+    else:
+        from waminfer_b200.stack import FFNStack
+
+        stack = FFNStack(shards, geo, device)
+    requests = [Request(geo, device, seed=i) for i in range(args.requests)]
+    stream = torch.cuda.Stream(device)
+
+    def step():
+        for req in requests:
+            if world > 1:
+                stack.enqueue_pass(req.x[0], req.out[0], req.time[0], reuse=req)
+                stack.enqueue_pass(req.x[1], req.out[1], req.time[1])
+            else:
+                stack.enqueue_request(req, stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize(device)
+    status = stack.plan.status()
+    if status:
+        raise RuntimeError(f"device status {status:#x} after warm-up")
+    # Collectives inside a captured graph when the backend allows it; eager otherwise.
+    graph, mode = None, "eager"
+    try:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        mode = "graph"
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        graph, mode = None, f"eager ({type(exc).__name__})"
+        torch.cuda.synchronize(device)
+
+    def run():
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+    torch.cuda.synchronize(device)
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        pass
+    barrier(world)
+    torch.cuda.synchronize(device)
+    with Clocks(uuid) as clocks, torch.cuda.stream(stream):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            run()
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    ms_step = max_over_ranks(start.elapsed_time(end) / args.steps, world, device)
+    flops_step = geo.request_flops() * args.requests
+    if rank == 0:
+        line = {
+            "metric": METRIC, "impl": "ours-tp", "value": flops_step / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "ms_per_request": ms_step / args.requests, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
+            "config": dict(config_dict(geo, args, 1), parallelism=f"tp{world} (h split, one all-reduce per layer)",
+                           requests_per_step=args.requests, capture=mode),
+            "clocks": clocks.summary(),
+            "gpu_launches": stack.launches_per_request() * args.requests * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        graph.reset()
+    del graph
+    stack.close()
+    if world > 1:
+        dist.barrier()
+
+
 def main():
     args = parse()
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.tp:
+            run_tp(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -297,6 +297,27 @@ typedef struct wamffn_stack_args {
 int wamffn_stack_run(wamffn_block_plan* plan, void* stream, const wamffn_stack_args* args);
 
 /* ------------------------------------------------------------------------
+ * Tensor-parallel FFN stack (the hidden dimension split across ranks).  The
+ * reference runs each FFN on one GPU (blocks.py:252-258 over ffn.py:96-107);
+ * this mode splits h column-wise for W_up / b_up and row-wise (over K) for
+ * W_down, so `plan` is created with d_hidden = h / world and args->weights
+ * hold this rank's slices (w_up [h/world, d], b_up [h/world], w_down
+ * [d, h/world], full b_down and mod).  Per layer the rank's split-K partials
+ * of the down projection are summed (split order) into reduce_buffer
+ * ([rows, d] fp32, caller-owned, rows = that layer's GEMM rows), then
+ * allreduce(user, reduce_buffer, rows * d, stream) is called on the host
+ * while the layer is enqueued: it must enqueue a sum over all ranks into the
+ * same buffer, ordered after the work already on `stream` and before the work
+ * enqueued on it afterwards (an NCCL all-reduce on that stream, or a
+ * torch.distributed one).  The bias, gated residual, history scatter and the
+ * next layer's norm then run once on the reduced sum, identically on every
+ * rank.  A non-zero return from allreduce aborts the call with that status.
+ * ---------------------------------------------------------------------- */
+typedef int (*wamffn_allreduce_fn)(void* user, float* buffer, int64_t count, void* stream);
+int wamffn_stack_run_tp(wamffn_block_plan* plan, void* stream, const wamffn_stack_args* args, float* reduce_buffer,
+                        wamffn_allreduce_fn allreduce, void* user);
+
+/* ------------------------------------------------------------------------
  * Token selection (select_tokens, approximation.py:55-67):
  *   score[r] = 2 sum|now - before| / max(sum(|now| + |before|), 1e-6)  (fp32)
  *   mandatory rows score +inf; the `count` best rows (stable descending, ties

@@ -52,7 +52,11 @@ EXPORTED_SYMBOLS = (
     "wamffn_pack_weight",
     "wamffn_trace_enable",
     "wamffn_stack_run",
+    "wamffn_stack_run_tp",
 )
+
+# int allreduce(void* user, float* buffer, int64_t count, void* stream)
+ALLREDUCE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p)
 
 LINEAR_GELU = 1
 WEIGHTS_PACKED = 2
@@ -196,6 +200,7 @@ def _declare(lib):
     lib.wamffn_pack_weight.argtypes = [vp, vp, vp, i, i]
     lib.wamffn_trace_enable.argtypes = [i, vp, i]
     lib.wamffn_stack_run.argtypes = [vp, vp, ctypes.POINTER(StackArgs)]
+    lib.wamffn_stack_run_tp.argtypes = [vp, vp, ctypes.POINTER(StackArgs), vp, ALLREDUCE_FN, vp]
     for name in EXPORTED_SYMBOLS:
         if name not in ("wamffn_last_error", "wamffn_launch_count"):
             getattr(lib, name).restype = i

@@ -771,7 +771,8 @@ int env_int(const char* name, int dflt) {
 }
 
 int block_configs(const wamffn_block_plan* plan, int rows, GemmConfig* up, GemmConfig* down) {
-  int rc = make_gemm_config(rows, plan->h, plan->d, default_splits(plan->h, plan->d, plan->sm_count), up);
+  // The up projection applies GELU in its epilogue: it never splits K.
+  int rc = make_gemm_config(rows, plan->h, plan->d, 1, up);
   if (rc) return rc;
   // Down projection: K = h is long and the output narrow, so the SMs are filled
   // with split-K (optionally x token groups).
@@ -1026,7 +1027,13 @@ int launch_pass(wamffn_block_plan* plan, const wamffn_stack_args* a, bool gather
 
 extern "C" {
 
-int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_args* a) {
+}  // extern "C"
+
+namespace {
+
+// Shared body of wamffn_stack_run and wamffn_stack_run_tp (allreduce != null).
+int stack_run_impl(wamffn_block_plan* plan, void* stream_, const wamffn_stack_args* a, float* reduce_buffer,
+                   wamffn_allreduce_fn allreduce, void* user) {
   if (!plan || !a || !a->weights) return fail(WAMFFN_ERR_INVALID, "null argument");
   if (a->layers < 1) return fail(WAMFFN_ERR_INVALID, "layers=%d", a->layers);
   if (a->seq < 1 || a->seq > plan->max_seq || a->seq > plan->max_rows)
@@ -1061,7 +1068,10 @@ int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_
   auto gathered_layer = [&](int l) { return gather && l >= a->first_gathered_layer; };
   auto layer_rows = [&](int l) { return gathered_layer(l) ? a->rows : a->seq; };
 
-  if (pass_usable(plan, a, gather)) return launch_pass(plan, a, gather, stream);
+  const bool tp = allreduce != nullptr;
+  if (tp && (!reduce_buffer || !aligned16(reduce_buffer)))
+    return fail(WAMFFN_ERR_INVALID, "the tensor-parallel stack needs a 16-byte aligned reduce buffer");
+  if (!tp && pass_usable(plan, a, gather)) return launch_pass(plan, a, gather, stream);
 
   // Prologue of the first layer: y = x, norm + gather into the activation buffer.
   NormParams n{};
@@ -1099,6 +1109,26 @@ int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_
     BoundaryParams b{};
     b.partial = plan->partial;
     b.splits = down.splits;
+    if (tp) {
+      // This rank's share of the down projection, summed over its splits,
+      // then over the ranks; the boundary reads the one reduced sum.
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(unsigned(rows), 1, 1);
+      cfg.blockDim = dim3(unsigned(row_threads(d)), 1, 1);
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, split_sum_kernel, static_cast<const float*>(plan->partial), down.splits,
+                                     rows, d, reduce_buffer));
+      g_launches.fetch_add(1, std::memory_order_relaxed);
+      const int arc = allreduce(user, reduce_buffer, int64_t(rows) * d, stream_);
+      if (arc) return fail(arc, "allreduce callback failed at layer %d (status %d)", l, arc);
+      b.partial = reduce_buffer;
+      b.splits = 1;
+    }
     b.m = rows;
     b.dim = d;
     b.seq = a->seq;
@@ -1139,6 +1169,20 @@ int wamffn_stack_run(wamffn_block_plan* plan, void* stream_, const wamffn_stack_
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   return WAMFFN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wamffn_stack_run(wamffn_block_plan* plan, void* stream, const wamffn_stack_args* a) {
+  return stack_run_impl(plan, stream, a, nullptr, nullptr, nullptr);
+}
+
+int wamffn_stack_run_tp(wamffn_block_plan* plan, void* stream, const wamffn_stack_args* a, float* reduce_buffer,
+                        wamffn_allreduce_fn allreduce, void* user) {
+  if (!allreduce) return fail(WAMFFN_ERR_INVALID, "allreduce callback is null");
+  return stack_run_impl(plan, stream, a, reduce_buffer, allreduce, user);
 }
 
 int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear) {

@@ -359,6 +359,24 @@ struct BoundaryParams {
   unsigned int* status;
 };
 
+// Sum of the split-K partials of one rank's down projection, in split order
+// ([splits, m, dim] -> [m, dim] fp32), ahead of the cross-rank reduction of
+// the tensor-parallel stack.  One CTA per row.
+__global__ void __launch_bounds__(kRowThreads) split_sum_kernel(const float* __restrict__ partial, int splits, int m,
+                                                              int dim, float* __restrict__ out) {
+  pdl_wait_prior();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+  const int row = blockIdx.x;
+  for (int v = threadIdx.x; v < (dim >> 2); v += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < splits; ++s) {
+      const float4 a = reinterpret_cast<const float4*>(partial + (size_t(s) * m + row) * dim)[v];
+      acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+    }
+    reinterpret_cast<float4*>(out + size_t(row) * dim)[v] = acc;
+  }
+}
+
 constexpr int kBoundarySplitsBatch = 2;  // split-K partials loaded per batch of independent loads
 
 // Dynamic shared memory: dim floats.

@@ -117,7 +117,9 @@ class FFNStack:
         self.weights, self.geo, self.device, self.eps = weights, geo, torch.device(device), eps
         # Tile-packed copies streamed by the GEMMs (one contiguous 16 KB block per tile).
         self.packed = [(pack_weight(w.w_up), pack_weight(w.w_down)) for w in weights]
-        self.plan = BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d, d_hidden=geo.h)
+        # d_hidden from the weights: a tensor-parallel rank holds h / world columns.
+        self.plan = BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d,
+                              d_hidden=weights[0].w_up.shape[0])
         self._pingpong = [torch.empty(geo.seq, geo.d, device=device, dtype=torch.bfloat16) for _ in range(2)]
         self._keep = []  # argument structs referenced by enqueued launches
         self._layer_array = (_lib.LayerWeights * len(weights))()
@@ -150,10 +152,7 @@ class FFNStack:
         a.eps = self.eps
         return a
 
-    def enqueue_pass(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
-        """Runs the L layers with one ``wamffn_stack_run`` (fused layer
-        boundaries); with `reuse`, layers 1.. gather its indices and read /
-        write its history."""
+    def _stack_args(self, x_in, x_final, time, reuse: "Request | None") -> "_lib.StackArgs":
         geo = self.geo
         a = _lib.StackArgs()
         a.layers = len(self.weights)
@@ -174,6 +173,13 @@ class FFNStack:
         a.x_out = x_final.data_ptr()
         a.eps = self.eps
         self._keep.append(a)
+        return a
+
+    def enqueue_pass(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
+        """Runs the L layers with one ``wamffn_stack_run`` (fused layer
+        boundaries); with `reuse`, layers 1.. gather its indices and read /
+        write its history."""
+        a = self._stack_args(x_in, x_final, time, reuse)
         _lib.check(_lib.lib().wamffn_stack_run(self.plan.handle, stream, ctypes.byref(a)))
 
     def enqueue_pass_blocks(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
