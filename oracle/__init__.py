@@ -10,6 +10,9 @@ sm_100a library or raise.
                        and native FFN, gather / scatter / gated residual).
 * ``oracle.reuse``  -- numpy restatement of TokenReuse (RGB mandatory mask,
                        capacity bucket) and select_tokens (score, stable top-k).
+* ``oracle.euler``  -- the 2F/4F Euler schedule over the FFN stack (fresh
+                       updates, cached residual replay, Euler step) on the
+                       fp32 FFN restatement.
 
 Parity pinning: both are checked against golden vectors produced by running the
 reference's own code in this container (``tests/golden/make_golden.py``:

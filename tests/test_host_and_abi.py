@@ -137,3 +137,22 @@ def test_request_geometry_and_flops():
     rows = geo.request_rows()
     assert len(rows) == 60 and rows[0] == 392 and rows[1] == 304 and rows[30:] == [392] * 30
     assert geo.request_flops() == 4 * 3072 * 14336 * (392 + 29 * 304 + 30 * 392)
+
+
+def test_euler_schedule_matches_oracle_schedule():
+    """2F runs the stack at updates 0 and 3; 4F adds 6 and 9 (decided after
+    update 3 from the coarse motion against the 0.05 m threshold)."""
+    from oracle import euler as oeuler
+    from waminfer_b200.approximation import MotionRefinement
+    from waminfer_b200.euler import MOTION_THRESHOLD_M, SCHEDULE, UPDATES
+
+    assert SCHEDULE == oeuler.SCHEDULE and UPDATES == oeuler.UPDATES == 10
+    for amplitude, nfe in ((0.1, 2), (0.05, 4), (0.02, 4), (0.0501, 2)):
+        r = MotionRefinement(lambda clean: amplitude, MOTION_THRESHOLD_M, SCHEDULE)
+        fresh = []
+        for k in range(UPDATES):
+            if r.full(k):
+                fresh.append(k)
+            if k == 3:
+                r.decide(None)
+        assert r.nfe == nfe and fresh == oeuler.fresh_updates(nfe)
