@@ -283,6 +283,87 @@ def _graph_ms_per_replay(fn, device, replays):
     return ms
 
 
+def reference_ffn_phase_ms(device, geo, weights, replays):
+    """The reference's own FFN phase on this GPU, per layer as its blocks run
+    it without attention: the FFN_RESIDUAL norm that folds the previous
+    layer's gated FFN output (``pre_attn_at_layer_for_compile``,
+    WAMInfer/blocks.py:189-203), the CROSS_RESIDUAL norm of the FFN input
+    (blocks.py:241-243, zero cross output), then
+    ``VideoAdapter.ffn_at_layer_for_compile`` (gather, PreparedFFN's cuBLASLt
+    plans, history scatter / concat, last-layer gate; blocks.py:246-272), and
+    the history stack of the reuse pass (runtime.py:263).  The WAMInfer
+    package is the unmodified reference installed in baseline/_ref (imported
+    through a stub parent package: its __init__ needs the absent openwam);
+    the cuBLASLt extension is the one built from its source there."""
+    import types
+    from types import SimpleNamespace
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "WAMInfer" / "blocks.py").exists():
+        raise FileNotFoundError("baseline/_ref/WAMInfer is not installed")
+    if "WAMInfer" not in sys.modules:
+        pkg = types.ModuleType("WAMInfer")
+        pkg.__path__ = [str(ref_root / "WAMInfer")]
+        sys.modules["WAMInfer"] = pkg
+    if str(ref_root) not in sys.path:
+        sys.path.insert(0, str(ref_root))
+    import wam_infer_ffn_v1 as ext
+    from WAMInfer import blocks as rblocks
+    from WAMInfer import ffn as rffn
+    from WAMInfer._triton_inference import CROSS_RESIDUAL, FFN_RESIDUAL, SELF_INPUT, modulated_norm
+
+    rffn._extension = lambda: ext  # the same extension, prebuilt from the reference's source
+    d, h = geo.d, geo.h
+    blocks = []
+    for w in weights:
+        kw = dict(device=device, dtype=torch.bfloat16)
+        ffn = torch.nn.Sequential(torch.nn.Linear(d, h, **kw), torch.nn.GELU(approximate="tanh"),
+                                  torch.nn.Linear(h, d, **kw)).eval()
+        with torch.no_grad():
+            ffn[0].weight.copy_(w.w_up)
+            ffn[0].bias.copy_(w.b_up)
+            ffn[2].weight.copy_(w.w_down)
+            ffn[2].bias.copy_(w.b_down)
+        blocks.append(SimpleNamespace(ffn=ffn, modulation=w.mod, norm2=SimpleNamespace(eps=1e-6)))
+    native = SimpleNamespace(dit=SimpleNamespace(blocks=blocks), num_layers=len(blocks), training=False)
+    vb = rblocks.VideoAdapter(native)
+    with torch.no_grad():
+        vb.ffn = rffn.PreparedFFN(vb)
+        vb.ffn.prepare(rows=tuple(sorted(set(geo.request_rows()))))
+    from waminfer_b200.stack import Request
+
+    req = Request(geo, device, seed=4242)
+    zero = torch.zeros(1, geo.seq, d, device=device, dtype=torch.bfloat16)
+    history = req.history_in[:, None]
+
+    def one_pass(x, time, reuse):
+        extras = {}
+        if reuse:
+            extras = dict(token_reuse=dict(n=geo.current, count=geo.count, cache=history),
+                          token_indices=req.indices, token_outputs=[])
+        state = SimpleNamespace(time_mod=time[None], extras=extras, hidden_states=x[None])
+        for layer, block in enumerate(blocks):
+            pending = state.extras.pop("_inference_ffn_residual", None)
+            update, previous = (None, None) if pending is None else pending
+            xs, _ = modulated_norm(state.hidden_states, update, block.modulation, previous, state.time_mod, None,
+                                   None, SELF_INPUT if pending is None else FFN_RESIDUAL, 1e-6)
+            xs, normalized = modulated_norm(xs, zero, block.modulation, None, state.time_mod, None, None,
+                                            CROSS_RESIDUAL, 1e-6)
+            vb.ffn_at_layer_for_compile(layer, state, normalized, xs)
+        if reuse:
+            torch.stack(state.extras["token_outputs"][1:])
+        return state.hidden_states
+
+    def request():
+        with torch.no_grad():
+            one_pass(req.x[0], req.time[0], True)
+            one_pass(req.x[1], req.time[1], False)
+
+    ms = _graph_ms_per_replay(request, device, replays)
+    vb.ffn.close()
+    return ms
+
+
 def gpu_baselines(device, geo, weights, replays=5):
     """Same-GPU baselines over one request's 60 layer passes (FFN GEMMs only,
     no norm / gather / scatter), CUDA-graph replayed:
@@ -306,6 +387,29 @@ def gpu_baselines(device, geo, weights, replays=5):
             F.linear(h, w.w_down, w.b_down)
 
     out["torch_native_ms_per_request"] = _graph_ms_per_replay(native, device, replays)
+
+    # The same GEMM-only work on this library's plans (up + bias + GELU, split-K
+    # down + bias), for a like-for-like comparison of the GEMM engines.
+    from waminfer_b200.ffn import Plan, pack_weight
+
+    packed = [(pack_weight(w.w_up), pack_weight(w.w_down)) for w in weights]
+    our_plans = {}
+    for m in set(rows):
+        hid = torch.empty(m, geo.h, device=device, dtype=torch.bfloat16)
+        our_plans[m] = (Plan(xs[m], packed[0][0], weights[0].b_up, True, True),
+                        Plan(hid, packed[0][1], weights[0].b_down, True, False))
+
+    def ours_gemms():
+        for i, m in enumerate(rows):
+            w, (wu, wd) = weights[i % layers], packed[i % layers]
+            up, down = our_plans[m]
+            down.run(up.run(xs[m], wu, w.b_up), wd, w.b_down)
+
+    out["ours_gemms_only_ms_per_request"] = _graph_ms_per_replay(ours_gemms, device, replays)
+    for up, down in our_plans.values():
+        up.close()
+        down.close()
+    del packed, our_plans
     ref_dir = ROOT / "baseline" / "_ref"
     if (ref_dir / "wam_infer_ffn_v1.so").exists():
         try:
@@ -331,6 +435,10 @@ def gpu_baselines(device, geo, weights, replays=5):
             del col, plans
         except Exception as exc:  # reported, not fatal: the product arm does not depend on it
             out["reference_cublaslt_error"] = f"{type(exc).__name__}: {exc}"
+        try:
+            out["reference_ffn_phase_ms_per_request"] = reference_ffn_phase_ms(device, geo, weights, replays)
+        except Exception as exc:  # reported, not fatal
+            out["reference_ffn_phase_error"] = f"{type(exc).__name__}: {exc}"
     else:
         out["reference_cublaslt_error"] = "baseline/_ref/wam_infer_ffn_v1.so not built"
     torch.cuda.synchronize(device)
@@ -452,7 +560,12 @@ def run_ours(args, world, rank, local):
         baselines["ours_ms_per_request"] = ms_request
         for key in ("torch_native", "reference_cublaslt"):
             if f"{key}_ms_per_request" in baselines:
-                baselines[f"speedup_vs_{key}"] = baselines[f"{key}_ms_per_request"] / ms_request
+                # GEMMs only on both sides (these baselines time no norm / gather / scatter).
+                baselines[f"gemms_only_speedup_vs_{key}"] = (baselines[f"{key}_ms_per_request"] /
+                                                             baselines["ours_gemms_only_ms_per_request"])
+        if "reference_ffn_phase_ms_per_request" in baselines:
+            # Whole FFN phase on both sides: norms, gather, GEMMs, scatter, gated residual.
+            baselines["speedup_vs_reference_ffn_phase"] = baselines["reference_ffn_phase_ms_per_request"] / ms_request
 
     launches = stack.launches_per_request() * args.requests * args.steps
     if rank == 0:
