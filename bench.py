@@ -364,6 +364,44 @@ def reference_ffn_phase_ms(device, geo, weights, replays):
     return ms
 
 
+def projection_timings(device, geo, replays):
+    """Attention-side projections of one block at M = 392 rows (packed QKV
+    3072 -> 9216, self-attention output, cross-attention query and output,
+    3072 -> 3072): this library's plans against torch's F.linear (cuBLAS, what
+    the reference calls, WAMInfer/blocks.py:204-240), 30 layers' worth of
+    distinct weights so that every call streams its weights from HBM."""
+    import torch.nn.functional as F
+
+    from waminfer_b200.ffn import Plan, pack_weight
+
+    g = torch.Generator(device=device).manual_seed(123)
+    m, d, layers = geo.seq, geo.d, 30
+    x = torch.randn(m, d, device=device, generator=g).to(torch.bfloat16)
+    out = {}
+    for name, n in (("qkv", 3 * d), ("self_out", d), ("cross_q", d), ("cross_out", d)):
+        ws = [(torch.randn(n, d, device=device, generator=g) * 0.02).to(torch.bfloat16) for _ in range(layers)]
+        b = (torch.randn(n, device=device, generator=g) * 0.01).to(torch.bfloat16)
+        packed = [pack_weight(w) for w in ws]
+        plan = Plan(x, packed[0], b, True, False)
+
+        def ours():
+            for w in packed:
+                plan.run(x, w, b)
+
+        def torch_linear():
+            for w in ws:
+                F.linear(x, w, b)
+
+        t_ours = _graph_ms_per_replay(ours, device, replays) / layers * 1e3
+        t_torch = _graph_ms_per_replay(torch_linear, device, replays) / layers * 1e3
+        flops = 2 * m * n * d
+        out[name] = {"ours_us": t_ours, "torch_us": t_torch, "speedup": t_torch / t_ours,
+                     "ours_tflops": flops / (t_ours * 1e-6) / 1e12, "split_k": plan.selected_configuration()[4]}
+        plan.close()
+        del ws, packed
+    return out
+
+
 def gpu_baselines(device, geo, weights, replays=5):
     """Same-GPU baselines over one request's 60 layer passes (FFN GEMMs only,
     no norm / gather / scatter), CUDA-graph replayed:
@@ -406,6 +444,10 @@ def gpu_baselines(device, geo, weights, replays=5):
             down.run(up.run(xs[m], wu, w.b_up), wd, w.b_down)
 
     out["ours_gemms_only_ms_per_request"] = _graph_ms_per_replay(ours_gemms, device, replays)
+    try:
+        out["projections_m392"] = projection_timings(device, geo, replays)
+    except Exception as exc:  # reported, not fatal
+        out["projections_error"] = f"{type(exc).__name__}: {exc}"
     for up, down in our_plans.values():
         up.close()
         down.close()

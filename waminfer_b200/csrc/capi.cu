@@ -151,7 +151,8 @@ bool pair_enabled() {
   return on;
 }
 
-int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, int groups = 1) {
+int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, int groups = 1,
+                     int smem_budget = kSmemLimit - kSmemReserve) {
   if (rows < 1 || rows > kMaxTokens * 4)
     return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d outside [1, %d]", rows, kMaxTokens * 4);
   if (groups < 1 || groups > 4) return fail(WAMFFN_ERR_UNSUPPORTED, "token groups=%d outside [1, 4]", groups);
@@ -204,7 +205,7 @@ int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, i
   c->tmem_cols = cols;
   // Shared memory: the activation ring (L2 hits, needs depth against the
   // lockstep bursts of all SMs) and the weight ring (HBM stream) share 227 KB.
-  const int budget = kSmemLimit - kSmemReserve;
+  const int budget = smem_budget;
   const int b_bytes = c->b_rows * kBlockK * 2;
   c->b_stages = (budget / 2) / b_bytes;
   if (c->b_stages > kMaxBStages) c->b_stages = kMaxBStages;
