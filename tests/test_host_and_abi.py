@@ -47,6 +47,12 @@ def test_abi_rejects_bad_arguments_without_a_gpu():
     assert lib.wamffn_select_tokens(None, ctypes.byref(sel)) == _lib.WAMFFN_ERR_INVALID
     with pytest.raises(_lib.WamffnError):
         _lib.check(lib.wamffn_block_run(None, None, None))
+    # Stack entry points: null plan / arguments, and the tensor-parallel hook is required.
+    stack = _lib.StackArgs(layers=1)
+    assert lib.wamffn_stack_run(None, None, ctypes.byref(stack)) == _lib.WAMFFN_ERR_INVALID
+    assert lib.wamffn_stack_run_tp(None, None, ctypes.byref(stack), None, _lib.ALLREDUCE_FN(), None) == \
+        _lib.WAMFFN_ERR_INVALID
+    assert b"allreduce" in lib.wamffn_last_error()
 
 
 def test_token_reuse_capacity_and_history(golden):

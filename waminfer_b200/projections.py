@@ -27,7 +27,7 @@ import torch.nn.functional as F
 from waminfer_b200.blocks import _parameter_signature
 from waminfer_b200.ffn import _IDS, _PLANS, Plan, pack_weight, prepared_linear
 
-# (attribute path on the block, packed names or None for a single Linear)
+# projection -> (attention module on the block, Linear names packed along the output features)
 PROJECTIONS = {
     "qkv": ("self_attn", ("q", "k", "v")),
     "self_out": ("self_attn", ("o",)),
@@ -67,7 +67,6 @@ class PreparedProjections:
         self.backbone = backbone
         self.weights = {}      # (layer, kind) -> tile-packed weight
         self.biases = {}       # (layer, kind) -> bias (zeros when the reference has none)
-        self.source = {}       # (layer, kind) -> row-major weight (fallback)
         self.signatures = {}
         self.plans = {}        # (layer, kind, rows) -> plan id
         self.keys = {}
@@ -102,7 +101,6 @@ class PreparedProjections:
                     self.weights[key] = pack_weight(weight)
                     self.biases[key] = bias.contiguous() if bias is not None else torch.zeros(
                         weight.shape[0], device=weight.device, dtype=weight.dtype)
-                    self.source[key] = (weight, bias)
                     self.signatures[key] = signature
                     changed = True
                 for m in rows:
@@ -148,7 +146,6 @@ class PreparedProjections:
         self.plans.clear()
         self.weights.clear()
         self.biases.clear()
-        self.source.clear()
         self.signatures.clear()
 
     def __del__(self):
