@@ -179,12 +179,17 @@ int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, i
       c->n_boxes = 1;
       c->tok_box = c->tok_pad / 2;
     } else {
-      c->tok_pad = (rows + 31) / 32 * 32;
-      c->mma_n0 = c->mma_n1 = c->tok_pad / 2;
+      // Two UMMAs with N multiples of 16 covering the rows with the least
+      // padding (392 -> 208 + 192, 304 -> 160 + 144).  Each CTA stages both
+      // halves in boxes of the larger height; the smaller box's extra rows are
+      // loaded but not read.
+      c->mma_n0 = ((rows + 1) / 2 + 15) / 16 * 16;
+      c->mma_n1 = (rows - c->mma_n0 + 15) / 16 * 16;
+      c->tok_pad = c->mma_n0 + c->mma_n1;
       c->n_boxes = 2;
-      c->tok_box = c->tok_pad / 4;
+      c->tok_box = c->mma_n0 / 2;
     }
-    c->b_rows = c->tok_pad / 2;
+    c->b_rows = c->n_boxes * c->tok_box;
   } else {
     c->tok_pad = (rows + 15) / 16 * 16;
     if (c->tok_pad <= 256) {

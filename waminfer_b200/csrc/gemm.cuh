@@ -212,8 +212,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t dst = smem_addr(ring + s * bytes + b * p.tok_box * kBlockK * 2);
             if constexpr (kGroup == 2) {
               // Box b feeds UMMA b: this CTA holds its rank's half of that UMMA's tokens.
-              tma_load_2d_pair(dst, &tm_x, fb, kx, tok_base + b * (2 * p.tok_box) + int(pair_rank) * p.tok_box,
-                               policy);
+              const int row = b == 0 ? int(pair_rank) * (p.mma_n0 / 2) : p.mma_n0 + int(pair_rank) * (p.mma_n1 / 2);
+              tma_load_2d_pair(dst, &tm_x, fb, kx, tok_base + row, policy);
             } else {
               tma_load_2d(dst, &tm_x, fb, kx, tok_base + b * p.tok_box, policy);
             }

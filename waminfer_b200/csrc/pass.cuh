@@ -498,8 +498,8 @@ __global__ void __launch_bounds__(kPassThreads, 1) stack_pass_kernel(const __gri
               } else {
                 for (int b = 0; b < C.n_boxes; ++b) {
                   const uint32_t dst = smem_addr(ring + s * slot_bytes + b * C.tok_box * kBlockK * 2);
-                  tma_load_2d_pair(dst, tm, fb, kb * kBlockK, b * (2 * C.tok_box) + int(pair_rank) * C.tok_box,
-                                   policy);
+                  const int row = b == 0 ? int(pair_rank) * (C.mma_n0 / 2) : C.mma_n0 + int(pair_rank) * (C.mma_n1 / 2);
+                  tma_load_2d_pair(dst, tm, fb, kb * kBlockK, row, policy);
                 }
               }
             }
