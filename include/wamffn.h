@@ -297,6 +297,19 @@ typedef struct wamffn_stack_args {
 int wamffn_stack_run(wamffn_block_plan* plan, void* stream, const wamffn_stack_args* args);
 
 /* ------------------------------------------------------------------------
+ * Self-test of the failure path.  No counterpart in the reference.  Launches
+ * one CTA on `stream` whose pipeline wait can never complete (a barrier no
+ * one arrives on), with a wait limit of `limit_cycles` SM cycles
+ * (1e3..1e9); the wait gives up, raises the CTA's abort flag and ORs
+ * WAMFFN_DEV_TIMEOUT into *status (a 4-byte aligned device word the caller
+ * cleared), a second role waiting on the same barrier leaves through the
+ * abort flag, and the kernel returns.  Every pipeline wait of the library's
+ * kernels ends this way after 4e9 cycles (2-4 s) instead of hanging; this lets
+ * a test observe the mechanism in milliseconds without faulting the GPU.
+ * ---------------------------------------------------------------------- */
+int wamffn_selftest_wait_timeout(void* stream, uint32_t* status, int64_t limit_cycles);
+
+/* ------------------------------------------------------------------------
  * Tensor-parallel FFN stack (the hidden dimension split across ranks).  The
  * reference runs each FFN on one GPU (blocks.py:252-258 over ffn.py:96-107);
  * this mode splits h column-wise for W_up / b_up and row-wise (over K) for

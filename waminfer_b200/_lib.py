@@ -41,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "wamffn_linear_configuration",
     "wamffn_linear_status",
     "wamffn_linear_run_static",
+    "wamffn_selftest_wait_timeout",
     "wamffn_ffn_run",
     "wamffn_modulated_norm",
     "wamffn_block_plan_create",
@@ -189,6 +190,7 @@ def _declare(lib):
     lib.wamffn_linear_configuration.argtypes = [vp, u32p, i]
     lib.wamffn_linear_status.argtypes = [vp, u32p, i]
     lib.wamffn_linear_run_static.argtypes = [i, vp, i, i, i, i, i, vp, vp, vp, vp, vp]
+    lib.wamffn_selftest_wait_timeout.argtypes = [vp, vp, ctypes.c_int64]
     lib.wamffn_ffn_run.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp]
     lib.wamffn_modulated_norm.argtypes = [vp, ctypes.POINTER(NormArgs)]
     lib.wamffn_block_plan_create.argtypes = [i, i, i, i, i, i, ctypes.POINTER(vp)]

@@ -19,6 +19,31 @@
 #include "select.cuh"
 #include "wamffn.h"
 
+namespace wamffn {
+
+// Thread 0 waits on a barrier no one arrives on, with a short limit; thread 32
+// waits on the same phase with a longer one and must leave through the abort
+// flag that thread 0 raises.
+__global__ void selftest_wait_timeout_kernel(unsigned int* status, long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_addr(&bar), 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    wait_bounded(smem_addr(&bar), 0u, &abort_flag, status, WAMFFN_DEV_TIMEOUT, limit);
+  } else if (threadIdx.x == 32) {
+    if (!wait_bounded(smem_addr(&bar), 0u, &abort_flag, nullptr, 0u, 4 * limit) && abort_flag)
+      atomicOr(status, kSelftestAbortSeen);
+  }
+  __syncthreads();
+}
+
+}  // namespace wamffn
+
 // Scratch of wamffn_linear_run_static, one copy per device shared by every
 // call: a status word in the first 256 bytes, then [splits, rows, n_out] fp32
 // split-K partials.
@@ -640,6 +665,18 @@ int wamffn_linear_run_static(int device, void* stream_, int rows, int n_out, int
   e.status = st;
   e.pdl = 1;
   return launch_epi(e, stream, pdl);
+}
+
+int wamffn_selftest_wait_timeout(void* stream, uint32_t* status, int64_t limit_cycles) {
+  if (!status || (reinterpret_cast<uintptr_t>(status) & 3u))
+    return fail(WAMFFN_ERR_INVALID, "status must be a non-null, 4-byte aligned device word");
+  if (limit_cycles < 1000 || limit_cycles > 1000000000ll)
+    return fail(WAMFFN_ERR_INVALID, "limit_cycles=%lld outside [1e3, 1e9]", (long long)limit_cycles);
+  selftest_wait_timeout_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<unsigned int*>(status), static_cast<long long>(limit_cycles));
+  WAMFFN_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
 }
 
 int wamffn_ffn_run(wamffn_linear_plan* up, wamffn_linear_plan* down, void* stream, const void* x,

@@ -17,6 +17,7 @@ namespace wamffn {
 // every pipeline stage): 4e9 cycles is 2-4 s at 1-2 GHz.
 constexpr long long kWaitLimitCycles = 4000000000ll;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s, for waits outside pipelines
+constexpr unsigned int kSelftestAbortSeen = 0x100u;  // self-test: a second waiter left through the abort flag
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -102,16 +103,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 
 // Waits until the phase of `bar` with the given parity has completed.
 // Gives up when *abort becomes non-zero (another role bailed out) or after
-// kWaitLimitNs; on a timeout it raises *abort and ORs `timeout_bit` into the
-// device status word.  Returns true on success.
+// `limit` SM cycles (kWaitLimitCycles unless a self-test asks for less); on a
+// timeout it raises *abort and ORs `timeout_bit` into the device status word.
+// Returns true on success.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int* abort,
-                                             unsigned int* status, unsigned int timeout_bit) {
+                                             unsigned int* status, unsigned int timeout_bit,
+                                             long long limit = kWaitLimitCycles) {
   if (mbar_test_wait(bar, parity)) return true;
   const long long t0 = clock64();
+  const uint32_t hint_ns = limit < kWaitLimitCycles ? 10000u : 1000000u;
   while (true) {
-    if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
+    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitLimitCycles) {
+    if (clock64() - t0 > limit) {
       *abort = 1;
       if (status) atomicOr(status, timeout_bit);
       return false;
