@@ -79,12 +79,18 @@ const char* wamffn_last_error(void);
 /* Number of kernels this library has launched in the process (all devices). */
 unsigned long long wamffn_launch_count(void);
 
-/* Phase trace of the GEMM kernels (profiling aid; no reference counterpart:
- * the reference relies on external Nsight traces).  With a device buffer of
- * `records` x 8 uint64 (word 0 of record 0 is the record counter, zeroed by the
- * caller), every GEMM CTA appends {tag, start, operands ready, MMAs issued,
- * accumulator ready, epilogue done, SM id, K blocks} in globaltimer ns.
- * buffer == NULL switches tracing off.  Synchronous; not for use in capture. */
+/* Phase trace of the GEMM and layer-boundary kernels (profiling aid; no
+ * reference counterpart: the reference relies on external Nsight traces).
+ * With a device buffer of `records` x 8 uint64 (word 0 of record 0 is the
+ * record counter, zeroed by the caller), every GEMM CTA appends {tag, start,
+ * operands ready, MMAs issued, accumulator ready, epilogue done, SM id,
+ * K blocks} and every layer-boundary CTA {tag, start, wait done, reduction
+ * done, reduction done, end, SM id, 0} in globaltimer ns; tag = CTA x |
+ * CTA y << 16 | kind << 32 (kind: the GEMM epilogue 0 GELU, 1 bias, 2 split-K
+ * partials; 7 layer boundary).  The persistent pass kernel writes record
+ * 1 + cta * 3 (layers + 1) + 3 layer + phase instead.  waminfer_b200/trace.py
+ * decodes the buffer.  buffer == NULL switches tracing off.  Synchronous; not
+ * for use in capture. */
 int wamffn_trace_enable(int device, void* buffer, int records);
 
 /* ------------------------------------------------------------------------
