@@ -82,6 +82,15 @@ class Clocks:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=self.file, stderr=subprocess.DEVNULL, start_new_session=True)
+            # nvidia-smi takes a moment to start on a multi-GPU box: begin the
+            # timed region only once it samples (bounded wait), so that short
+            # regions still get samples; earlier lines are dropped.
+            deadline = time.time() + 10.0
+            while time.time() < deadline and self.proc.poll() is None:
+                if Path(self.file.name).stat().st_size > 0:
+                    break
+                time.sleep(0.02)
+            self.skip = len(Path(self.file.name).read_text().splitlines())
         except Exception:
             self.proc = None
         return self
@@ -99,7 +108,7 @@ class Clocks:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
         rows = []
-        for line in Path(self.file.name).read_text().splitlines():
+        for line in Path(self.file.name).read_text().splitlines()[getattr(self, "skip", 0):]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
                 continue
