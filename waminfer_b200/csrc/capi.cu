@@ -954,12 +954,12 @@ int pass_down_splits(const wamffn_block_plan* plan) {
 bool pass_usable(const wamffn_block_plan* plan, const wamffn_stack_args* a, bool gather) {
   static const bool on = env_flag("WAMFFN_PASS", false);
   if (!on || plan->pass_ctas < 2 || a->layers > kPassMaxLayers) return false;
-  if (plan->d > kPassRowThreads * kPassRowVec * 8 || plan->d % 256 || plan->h % 256) return false;
+  if (plan->d > kPassEpiThreads * 8 || plan->d % 256 || plan->h % 256) return false;
   if (!pair_enabled()) return false;
   const int npairs = plan->pass_ctas / 2;
   if (plan->h / 256 > npairs) return false;
   const int row_limit = a->seq > a->rows ? a->seq : a->rows;
-  if (row_limit > kPassRowSlots * kPassRowGroups * plan->pass_ctas) return false;
+  if (row_limit > kPassRowSlots * plan->pass_ctas) return false;
   return true;
 }
 

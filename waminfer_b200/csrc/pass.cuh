@@ -28,8 +28,8 @@
 //   warp 2        activation TMA producer
 //   warp 3        idle
 //   warps 4..15   GEMM epilogues (warp w reads TMEM lanes 32*(w%4).., every third
-//                 column chunk) and the row phases (three groups of four warps,
-//                 one row per group at a time)
+//                 column chunk) and the row phases (one row at a time, thread t
+//                 owning the row's 16-byte vector t, as in the row kernels)
 //
 // The arithmetic is the multi-kernel stack's, operation for operation: the
 // same UMMA sequence per tile, the same split-K slices and reduction order, and
@@ -48,15 +48,11 @@ namespace wamffn {
 
 constexpr int kPassThreads = 512;
 constexpr int kPassMaxLayers = 48;
-constexpr int kPassRowGroups = 3;
-constexpr int kPassRowThreads = 128;
-constexpr int kPassRowVec = 3;         // 16-byte vectors per row thread: d <= 3072
 constexpr int kPassEpiThreads = 384;   // warps 4..15
 constexpr int kPassEpiBarrier = 1;     // named barrier of the epilogue warps
-constexpr int kPassRowBarrier0 = 2;    // named barriers 2..4: one per row group
 constexpr int kPassTransposeBytes = 12 * 32 * 32 * 2;  // per-warp bf16 transpose tiles
 constexpr uint32_t kPassTmemCols = 512;
-constexpr int kPassRowSlots = 4;       // rows per row group: max(seq, rows) <= 12 * CTAs
+constexpr int kPassRowSlots = 4;       // rows per CTA: max(seq, rows) <= 4 * CTAs; d <= 8 * 384
 
 // GEMM geometry of one row count (the pass has at most two: all rows, gathered rows).
 struct PassClass {
@@ -164,31 +160,23 @@ __device__ __forceinline__ bool pass_wait(const PassParams& p, const unsigned in
   return true;
 }
 
-// Row reduction in the order of block_sum over the 384-thread row kernels:
-// per-virtual-thread sums (`local[s]` belongs to virtual thread tg + 128 s),
-// a shuffle tree per virtual warp, then the virtual warps in index order.
-__device__ __forceinline__ float pass_row_sum(const float (&local)[3], float* red, int bar_id, int nvw) {
+// Sum over the 12 epilogue warps in the order of block_sum (rowops.cuh): a
+// shuffle tree per warp, then the warps in index order; warps beyond the
+// row's vectors contribute zeros, as the row kernels' missing warps do.
+__device__ __forceinline__ float pass_row_sum(float v, float* red, int nwarps) {
   const int lane = threadIdx.x & 31;
-  const int wg = (threadIdx.x >> 5) & 3;  // warp within the row group
-  float v[3];
+  const int ew = (threadIdx.x >> 5) - 4;  // epilogue warp 0..11
 #pragma unroll
-  for (int s = 0; s < 3; ++s) {
-    v[s] = local[s];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v[s] += __shfl_xor_sync(0xffffffffu, v[s], o);
-  }
-  named_sync(bar_id, kPassRowThreads);  // red[] may still be read by a previous reduction
-  if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < 3; ++s) red[wg + 4 * s] = v[s];
-  }
-  named_sync(bar_id, kPassRowThreads);
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  named_sync(kPassEpiBarrier, kPassEpiThreads);  // red[] may still be read by a previous reduction
+  if (lane == 0) red[ew] = v;
+  named_sync(kPassEpiBarrier, kPassEpiThreads);
   float total = 0.f;
-  for (int w = 0; w < nvw; ++w) total += red[w];
+  for (int w = 0; w < nwarps; ++w) total += red[w];
   return total;
 }
 
-// Gather bookkeeping of one row slot of a row group, computed once per pass
+// Gather bookkeeping of one row slot of this CTA, computed once per pass
 // (the gather list is an input of the whole pass): the last entry of the list
 // naming the row (its GEMM row in a gathered layer), the entries naming it
 // (the slots its normalised row is copied to) and whether the list entry at
@@ -200,16 +188,16 @@ struct PassRowSlot {
   int matches[kMaxMatches];
 };
 
-__device__ void pass_row_setup(const PassParams& p, int r, int tg, int bar_id, PassRowSlot* slot) {
+__device__ void pass_row_setup(const PassParams& p, int r, int et, PassRowSlot* slot) {
   const int m = p.cls[1].rows;
-  if (tg == 0) {
+  if (et == 0) {
     slot->j_idx = -1;
     slot->n_match = 0;
     slot->bad_slot = 0;
   }
-  named_sync(bar_id, kPassRowThreads);
+  named_sync(kPassEpiBarrier, kPassEpiThreads);
   if (p.idx != nullptr) {
-    if (tg == 0 && r < m) {
+    if (et == 0 && r < m) {
       const long long v = load_index(p.idx, p.idx_bytes, r);
       if (v < 0 || v >= p.seq) {
         slot->bad_slot = 1;
@@ -217,7 +205,7 @@ __device__ void pass_row_setup(const PassParams& p, int r, int tg, int bar_id, P
       }
     }
     if (r < p.seq) {
-      for (int j = tg; j < m; j += kPassRowThreads) {
+      for (int j = et; j < m; j += kPassEpiThreads) {
         if (load_index(p.idx, p.idx_bytes, j) == r) {
           atomicMax(&slot->j_idx, j);
           const int k = atomicAdd(&slot->n_match, 1);
@@ -227,17 +215,17 @@ __device__ void pass_row_setup(const PassParams& p, int r, int tg, int bar_id, P
       }
     }
   }
-  named_sync(bar_id, kPassRowThreads);
+  named_sync(kPassEpiBarrier, kPassEpiThreads);
   // A gathered layer neither computes nor caches this row: its FFN output is undefined.
-  if (tg == 0 && p.idx != nullptr && p.first_gathered < p.layers && r < p.seq && slot->j_idx < 0 &&
+  if (et == 0 && p.idx != nullptr && p.first_gathered < p.layers && r < p.seq && slot->j_idx < 0 &&
       r >= p.cache_rows)
     atomicOr(p.status, WAMFFN_DEV_BAD_INDEX);
 }
 
-// One row (or gather slot) `r` of phase R(l), by the 128 threads of a row group.
-// Thread tg owns the 16-byte vectors v = tg + 128 jv of the row.
-__device__ void pass_row(const PassParams& p, int l, int r, int tg, int bar_id, float* red,
-                         const PassRowSlot* slot) {
+// One row (or gather slot) `r` of phase R(l) by the 384 epilogue threads:
+// thread et owns the 16-byte vector et of the row, as in the row kernels, so
+// every value and every reduction matches the three-kernel stack bit for bit.
+__device__ void pass_row(const PassParams& p, int l, int r, int et, float* red, const PassRowSlot* slot) {
   const int d = p.d;
   const int nvec = d >> 3;
   const bool has_next = l < p.layers;   // a layer follows: norm + gather for it
@@ -246,39 +234,28 @@ __device__ void pass_row(const PassParams& p, int l, int r, int tg, int bar_id, 
   const int next_m = has_next ? p.cls[pass_class(p, l)].rows : 0;
   const bool cur_gathered = has_prev && l - 1 >= p.first_gathered;
   const int cur_m = has_prev ? p.cls[pass_class(p, l - 1)].rows : 0;
+  const bool active = et < nvec;
+  const int e = et * 8;
 
   // Invalid entries of the next layer's list: the GEMM reads zeros there.
-  if (next_gathered && r < next_m && slot->bad_slot) {
-    for (int k = tg; k < nvec; k += kPassRowThreads)
-      *reinterpret_cast<uint4*>(p.gathered + size_t(r) * d + k * 8) = make_uint4(0, 0, 0, 0);
-  }
+  if (next_gathered && r < next_m && slot->bad_slot && active)
+    *reinterpret_cast<uint4*>(p.gathered + size_t(r) * d + e) = make_uint4(0, 0, 0, 0);
   if (r >= p.seq) return;
   const int row = r;
   const int j = !has_prev ? row : (cur_gathered ? slot->j_idx : (row < cur_m ? row : -1));
   const bool cached_row = cur_gathered && row < p.cache_rows;
 
-  // The row after layer l-1 (or the input row): x = y + gate * (down + bias).
-  uint4 xp[kPassRowVec];  // the row after the update, bf16 (exact: every value is rounded to bf16)
-  float local[3] = {0.f, 0.f, 0.f};
-  if (!has_prev) {
-#pragma unroll
-    for (int jv = 0; jv < kPassRowVec; ++jv) {
-      const int v = tg + kPassRowThreads * jv;
-      if (v < nvec) {
-        xp[jv] = *reinterpret_cast<const uint4*>(p.x + size_t(row) * d + v * 8);
-        *reinterpret_cast<uint4*>(p.y + size_t(row) * d + v * 8) = xp[jv];
-      }
-    }
-  } else {
-    const int lp = l - 1;
-    const size_t slot_off = cur_gathered ? size_t(lp - p.first_gathered) * p.cache_rows * d : 0;
-    // One batch of independent loads per vector: the residual, the gate's
-    // modulation and time rows, the bias and four splits' partials.
-#pragma unroll
-    for (int jv = 0; jv < kPassRowVec; ++jv) {
-      const int v = tg + kPassRowThreads * jv;
-      if (v >= nvec) continue;
-      const int e = v * 8;
+  float x[8];
+  float local = 0.f;
+  if (active) {
+    if (!has_prev) {
+      load8(p.x + size_t(row) * d + e, x);
+      store8(p.y + size_t(row) * d + e, x);
+    } else {
+      // Independent loads: the residual, the gate's modulation and time rows,
+      // the bias, then the partials three splits at a time (register budget).
+      const int lp = l - 1;
+      const size_t slot_off = cur_gathered ? size_t(lp - p.first_gathered) * p.cache_rows * d : 0;
       const uint4 y_pk = *reinterpret_cast<const uint4*>(p.y + size_t(row) * d + e);
       const uint4 g_pk = modulation8_packed(p.mod[lp], p.time, p.ts, row, 5, d, e);
       float o[8];
@@ -289,10 +266,10 @@ __device__ void pass_row(const PassParams& p, int l, int r, int tg, int bar_id, 
         float acc[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int s0 = 0; s0 < p.down_splits; s0 += 4) {
-          float4 part[4][2];
+        for (int s0 = 0; s0 < p.down_splits; s0 += 3) {
+          float4 part[3][2];
 #pragma unroll
-          for (int s = 0; s < 4; ++s) {
+          for (int s = 0; s < 3; ++s) {
             if (s0 + s < p.down_splits) {
               const float4* src = reinterpret_cast<const float4*>(base + (s0 + s) * split_stride);
               part[s][0] = src[0];
@@ -300,7 +277,7 @@ __device__ void pass_row(const PassParams& p, int l, int r, int tg, int bar_id, 
             }
           }
 #pragma unroll
-          for (int s = 0; s < 4; ++s) {
+          for (int s = 0; s < 3; ++s) {
             if (s0 + s < p.down_splits) {
               acc[0] += part[s][0].x; acc[1] += part[s][0].y; acc[2] += part[s][0].z; acc[3] += part[s][0].w;
               acc[4] += part[s][1].x; acc[5] += part[s][1].y; acc[6] += part[s][1].z; acc[7] += part[s][1].w;
@@ -318,71 +295,50 @@ __device__ void pass_row(const PassParams& p, int l, int r, int tg, int bar_id, 
         for (int i = 0; i < 8; ++i) o[i] = 0.f;
       }
       if (cached_row && p.cache_out != nullptr) store8(p.cache_out + slot_off + size_t(row) * d + e, o);
-      float g[8], y[8], x[8];
+      float g[8], y[8];
       unpack8(g_pk, g);
       unpack8(y_pk, y);
 #pragma unroll
       for (int i = 0; i < 8; ++i) x[i] = bf16_round(y[i] + bf16_round(g[i] * o[i]));
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&xp[jv]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
-      *reinterpret_cast<uint4*>((has_next ? p.y : p.x_out) + size_t(row) * d + e) = xp[jv];
+      store8((has_next ? p.y : p.x_out) + size_t(row) * d + e, x);
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) local += x[i];
   }
   if (!has_next) return;
-#pragma unroll
-  for (int jv = 0; jv < kPassRowVec; ++jv) {
-    const int v = tg + kPassRowThreads * jv;
-    if (v < nvec) {
-      float x[8];
-      unpack8(xp[jv], x);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) local[jv % 3] += x[i];
-    }
-  }
 
   // LayerNorm + adaLN (FFN shift / scale slots 3 and 4 of layer l), gather.
-  const int nvw = min(12, (nvec + 31) >> 5);
-  const float mean = pass_row_sum(local, red, bar_id, nvw) / float(d);
-  local[0] = local[1] = local[2] = 0.f;
-#pragma unroll
-  for (int jv = 0; jv < kPassRowVec; ++jv) {
-    const int v = tg + kPassRowThreads * jv;
-    if (v >= nvec) break;
-    float x[8];
-    unpack8(xp[jv], x);
+  // The modulation rows are requested before the two reductions.
+  uint4 sh_pk = make_uint4(0, 0, 0, 0), sc_pk = make_uint4(0, 0, 0, 0);
+  if (active) {
+    sh_pk = modulation8_packed(p.mod[l], p.time, p.ts, row, 3, d, e);
+    sc_pk = modulation8_packed(p.mod[l], p.time, p.ts, row, 4, d, e);
+  }
+  const int nwarps = (nvec + 31) >> 5;
+  const float mean = pass_row_sum(local, red, nwarps) / float(d);
+  local = 0.f;
+  if (active) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float c = x[i] - mean;
-      local[jv % 3] += c * c;
+      local += c * c;
     }
   }
-  if (tg == 0 && bar_id == kPassRowBarrier0)
-    if (unsigned long long* rec = pass_trace(p, l, 0)) rec[4] = globaltimer_ns();
-  const float var = pass_row_sum(local, red, bar_id, nvw) / float(d);
+  const float var = pass_row_sum(local, red, nwarps) / float(d);
   const float rstd = rsqrtf(var + p.eps);
+  if (!active) return;
   // Gather slots of the next layer that read this row: its own index
   // (ungathered layer) or the list entries naming it.
   const int nm = next_gathered ? (slot->n_match < kMaxMatches ? slot->n_match : kMaxMatches) : (row < next_m ? 1 : 0);
+  float n[8], shift[8], scale[8];
+  unpack8(sh_pk, shift);
+  unpack8(sc_pk, scale);
 #pragma unroll
-  for (int jv = 0; jv < kPassRowVec; ++jv) {
-    const int v = tg + kPassRowThreads * jv;
-    if (v >= nvec) break;
-    const int e = v * 8;
-    float n[8], shift[8], scale[8];
-    modulation8(p.mod[l], p.time, p.ts, row, 3, d, e, shift);
-    modulation8(p.mod[l], p.time, p.ts, row, 4, d, e, scale);
-    float x[8];
-    unpack8(xp[jv], x);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float s1 = bf16_round(1.0f + scale[i]);
-      n[i] = bf16_round(bf16_round((x[i] - mean) * rstd) * s1) + shift[i];
-    }
-    for (int k = 0; k < nm; ++k) store8(p.gathered + size_t(next_gathered ? slot->matches[k] : row) * d + e, n);
+  for (int i = 0; i < 8; ++i) {
+    const float s1 = bf16_round(1.0f + scale[i]);
+    n[i] = bf16_round(bf16_round((x[i] - mean) * rstd) * s1) + shift[i];
   }
-  if (tg == 0 && bar_id == kPassRowBarrier0)
-    if (unsigned long long* rec = pass_trace(p, l, 0)) rec[6] = globaltimer_ns();
+  for (int k = 0; k < nm; ++k) store8(p.gathered + size_t(next_gathered ? slot->matches[k] : row) * d + e, n);
 }
 
 __global__ void __launch_bounds__(kPassThreads, 1) stack_pass_kernel(const __grid_constant__ PassParams p) {
@@ -391,8 +347,8 @@ __global__ void __launch_bounds__(kPassThreads, 1) stack_pass_kernel(const __gri
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_verdict;
-  __shared__ float s_red[kPassRowGroups][16];
-  __shared__ PassRowSlot s_rows[kPassRowGroups][kPassRowSlots];
+  __shared__ float s_red[16];
+  __shared__ PassRowSlot s_rows[kPassRowSlots];
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -600,16 +556,13 @@ __global__ void __launch_bounds__(kPassThreads, 1) stack_pass_kernel(const __gri
     const int et = threadIdx.x - 128;  // 0..383
     const int ew = warp - 4;           // 0..11
     const int q = warp & 3;            // TMEM lane quarter of this warp
-    const int group = ew >> 2;         // 0..2: column-chunk group and row group
-    const int tg = threadIdx.x & (kPassRowThreads - 1);
-    const int row_bar = kPassRowBarrier0 + group;
+    const int group = ew >> 2;         // 0..2: TMEM column-chunk group
     uint32_t item = 0;
-    // Rows of this row group: blockIdx.x + nctas * (group + 3 k), k < kPassRowSlots.
-    const int row_stride = int(nctas) * kPassRowGroups;
+    // Rows of this CTA: blockIdx.x + nctas k, k < kPassRowSlots.
     const int row_limit = max(p.seq, p.cls[1].rows);
     for (int k = 0; k < kPassRowSlots; ++k) {
-      const int r = blockIdx.x + int(nctas) * group + k * row_stride;
-      if (r < row_limit) pass_row_setup(p, r, tg, row_bar, &s_rows[group][k]);
+      const int r = blockIdx.x + int(nctas) * k;
+      if (r < row_limit) pass_row_setup(p, r, et, &s_rows[k]);
     }
     for (int l = 0; l <= p.layers; ++l) {
       // ---- R(l): needs every CTA's partials of D(l-1).
@@ -628,9 +581,8 @@ __global__ void __launch_bounds__(kPassThreads, 1) stack_pass_kernel(const __gri
       {
         const int limit = max(p.seq, l < p.layers ? p.cls[pass_class(p, l)].rows : 0);
         for (int k = 0; k < kPassRowSlots; ++k) {
-          const int r = blockIdx.x + int(nctas) * group + k * row_stride;
-          if (r < limit)
-            pass_row(p, l, r, tg, row_bar, s_red[group], &s_rows[group][k]);
+          const int r = blockIdx.x + int(nctas) * k;
+          if (r < limit) pass_row(p, l, r, et, s_red, &s_rows[k]);
         }
       }
       if (l == p.layers) break;
