@@ -10,6 +10,9 @@ with cache scatter) and 30 layers at update 3 over all 392 rows.  d = 3072,
 hidden = 14336, tanh-GELU, seeded synthetic weights and activations.
 Requests are independent: with N GPUs each rank runs its own R requests (weak
 scaling, no data-path collective; one all-reduce of the elapsed time only).
+On each GPU the R requests run over --lanes concurrent lanes (streams with
+their own scratch over the shared weights; the headline throughput); the same
+requests on one lane give the per-request latency (`latency_ms_per_request`).
 """
 
 from __future__ import annotations
@@ -44,7 +47,11 @@ def parse():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--requests", type=int, default=16, help="requests per GPU per step")
+    p.add_argument("--requests", type=int, default=24, help="requests per GPU per step")
+    p.add_argument("--lanes", type=int, default=6,
+                   help="concurrent request lanes per GPU (streams with their own scratch, shared weights)")
+    p.add_argument("--down-splits", type=int, default=1,
+                   help="split-K of the down projection when lanes > 1 (one lane uses the SM-filling heuristic)")
     p.add_argument("--layers", type=int, default=30)
     p.add_argument("--cpu-sample-layers", type=int, default=2)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -219,6 +226,7 @@ def config_dict(geo, args, world):
         "rows_update0": [geo.seq] + [geo.reuse_rows] * (geo.layers - 1), "rows_update3": geo.seq,
         "requests_per_gpu_per_step": args.requests, "requests_per_step": args.requests * world,
         "parallelism": f"request-parallel x{world}",
+        "lanes_per_gpu": args.lanes, "down_splits": args.down_splits if args.lanes > 1 else "heuristic",
         "l2": "no flush needed: each pass streams 30 x 176 MB of weights through the 126 MB L2",
     }
 
@@ -292,7 +300,7 @@ def _graph_ms_per_replay(fn, device, replays):
     return ms
 
 
-def reference_ffn_phase_ms(device, geo, weights, replays):
+def reference_ffn_phase_ms(device, geo, weights, replays, lanes=1):
     """The reference's own FFN phase on this GPU, per layer as its blocks run
     it without attention: the FFN_RESIDUAL norm that folds the previous
     layer's gated FFN output (``pre_attn_at_layer_for_compile``,
@@ -303,7 +311,12 @@ def reference_ffn_phase_ms(device, geo, weights, replays):
     the history stack of the reuse pass (runtime.py:263).  The WAMInfer
     package is the unmodified reference installed in baseline/_ref (imported
     through a stub parent package: its __init__ needs the absent openwam);
-    the cuBLASLt extension is the one built from its source there."""
+    the cuBLASLt extension is the one built from its source there.
+
+    Returns the latency (one request per replay) and, with lanes > 1, the
+    throughput of `lanes` requests run concurrently on as many streams, each
+    lane a VideoAdapter with its own PreparedFFN (plans and workspaces are
+    per model in the reference, ffn.py:5-6) over the shared weights."""
     import types
     from types import SimpleNamespace
 
@@ -335,42 +348,62 @@ def reference_ffn_phase_ms(device, geo, weights, replays):
             ffn[2].bias.copy_(w.b_down)
         blocks.append(SimpleNamespace(ffn=ffn, modulation=w.mod, norm2=SimpleNamespace(eps=1e-6)))
     native = SimpleNamespace(dit=SimpleNamespace(blocks=blocks), num_layers=len(blocks), training=False)
-    vb = rblocks.VideoAdapter(native)
-    with torch.no_grad():
-        vb.ffn = rffn.PreparedFFN(vb)
-        vb.ffn.prepare(rows=tuple(sorted(set(geo.request_rows()))))
     from waminfer_b200.stack import Request
 
-    req = Request(geo, device, seed=4242)
     zero = torch.zeros(1, geo.seq, d, device=device, dtype=torch.bfloat16)
-    history = req.history_in[:, None]
 
-    def one_pass(x, time, reuse):
-        extras = {}
-        if reuse:
-            extras = dict(token_reuse=dict(n=geo.current, count=geo.count, cache=history),
-                          token_indices=req.indices, token_outputs=[])
-        state = SimpleNamespace(time_mod=time[None], extras=extras, hidden_states=x[None])
-        for layer, block in enumerate(blocks):
-            pending = state.extras.pop("_inference_ffn_residual", None)
-            update, previous = (None, None) if pending is None else pending
-            xs, _ = modulated_norm(state.hidden_states, update, block.modulation, previous, state.time_mod, None,
-                                   None, SELF_INPUT if pending is None else FFN_RESIDUAL, 1e-6)
-            xs, normalized = modulated_norm(xs, zero, block.modulation, None, state.time_mod, None, None,
-                                            CROSS_RESIDUAL, 1e-6)
-            vb.ffn_at_layer_for_compile(layer, state, normalized, xs)
-        if reuse:
-            torch.stack(state.extras["token_outputs"][1:])
-        return state.hidden_states
-
-    def request():
+    def make_lane(seed):
+        vb = rblocks.VideoAdapter(native)
         with torch.no_grad():
-            one_pass(req.x[0], req.time[0], True)
-            one_pass(req.x[1], req.time[1], False)
+            vb.ffn = rffn.PreparedFFN(vb)
+            vb.ffn.prepare(rows=tuple(sorted(set(geo.request_rows()))))
+        req = Request(geo, device, seed=seed)
+        history = req.history_in[:, None]
 
-    ms = _graph_ms_per_replay(request, device, replays)
-    vb.ffn.close()
-    return ms
+        def one_pass(x, time, reuse):
+            extras = {}
+            if reuse:
+                extras = dict(token_reuse=dict(n=geo.current, count=geo.count, cache=history),
+                              token_indices=req.indices, token_outputs=[])
+            state = SimpleNamespace(time_mod=time[None], extras=extras, hidden_states=x[None])
+            for layer, block in enumerate(blocks):
+                pending = state.extras.pop("_inference_ffn_residual", None)
+                update, previous = (None, None) if pending is None else pending
+                xs, _ = modulated_norm(state.hidden_states, update, block.modulation, previous, state.time_mod,
+                                       None, None, SELF_INPUT if pending is None else FFN_RESIDUAL, 1e-6)
+                xs, normalized = modulated_norm(xs, zero, block.modulation, None, state.time_mod, None, None,
+                                                CROSS_RESIDUAL, 1e-6)
+                vb.ffn_at_layer_for_compile(layer, state, normalized, xs)
+            if reuse:
+                torch.stack(state.extras["token_outputs"][1:])
+            return state.hidden_states
+
+        def request():
+            with torch.no_grad():
+                one_pass(req.x[0], req.time[0], True)
+                one_pass(req.x[1], req.time[1], False)
+
+        return vb, request
+
+    lanes_ = [make_lane(4242 + i) for i in range(lanes)]
+    out = {"latency_ms": _graph_ms_per_replay(lanes_[0][1], device, replays)}
+    if lanes > 1:
+        streams = [torch.cuda.Stream(device) for _ in range(lanes)]
+
+        def concurrent():
+            origin = torch.cuda.current_stream(device)
+            for st in streams:
+                st.wait_stream(origin)
+            for st, (_, fn) in zip(streams, lanes_):
+                with torch.cuda.stream(st):
+                    fn()
+            for st in streams:
+                origin.wait_stream(st)
+
+        out["lanes_ms_per_request"] = _graph_ms_per_replay(concurrent, device, replays) / lanes
+    for vb, _ in lanes_:
+        vb.ffn.close()
+    return out
 
 
 def projection_timings(device, geo, replays):
@@ -411,7 +444,7 @@ def projection_timings(device, geo, replays):
     return out
 
 
-def gpu_baselines(device, geo, weights, replays=5):
+def gpu_baselines(device, geo, weights, replays=5, lanes=1):
     """Same-GPU baselines over one request's 60 layer passes (FFN GEMMs only,
     no norm / gather / scatter), CUDA-graph replayed:
     * torch native Linear -> GELU(tanh) -> Linear (what the reference runs on
@@ -487,7 +520,11 @@ def gpu_baselines(device, geo, weights, replays=5):
         except Exception as exc:  # reported, not fatal: the product arm does not depend on it
             out["reference_cublaslt_error"] = f"{type(exc).__name__}: {exc}"
         try:
-            out["reference_ffn_phase_ms_per_request"] = reference_ffn_phase_ms(device, geo, weights, replays)
+            phase = reference_ffn_phase_ms(device, geo, weights, replays, lanes)
+            out["reference_ffn_phase_ms_per_request"] = phase["latency_ms"]
+            if "lanes_ms_per_request" in phase:
+                out["reference_ffn_phase_lanes_ms_per_request"] = phase["lanes_ms_per_request"]
+                out["reference_ffn_phase_lanes"] = lanes
         except Exception as exc:  # reported, not fatal
             out["reference_ffn_phase_error"] = f"{type(exc).__name__}: {exc}"
     else:
@@ -515,27 +552,32 @@ def run_ours(args, world, rank, local):
     pk, pk_kind = peaks()
     geo = Geometry(layers=args.layers)
     weights = make_weights(geo.layers, geo.d, geo.h, device, seed=0)
-    stack = FFNStack(weights, geo, device)
-    history = None
-    requests = []
-    for i in range(args.requests):
-        req = Request(geo, device, seed=rank * 100_000 + i, history_in=history)
-        requests.append(req)
+    if args.lanes < 1:
+        raise SystemExit("--lanes must be at least 1")
+    stack = FFNStack(weights, geo, device, lanes=args.lanes)
+    requests = [Request(geo, device, seed=rank * 100_000 + i) for i in range(args.requests)]
     stream = torch.cuda.Stream(device)
     handle = stream.cuda_stream
 
-    # Eager warm-up (also checks the device status word), then capture R requests.
-    with torch.cuda.stream(stream):
-        for req in requests:
-            stack.enqueue_request(req, handle)
-    torch.cuda.synchronize(device)
-    status = stack.plan.status()
-    if status:
-        raise RuntimeError(f"device status {status:#x} after warm-up")
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for req in requests:
-            stack.enqueue_request(req, handle)
+    def capture(lanes, splits):
+        # Eager warm-up (also checks the device status words), then capture the
+        # R requests over `lanes` lanes into one graph.
+        stack.set_down_splits(splits)
+        with torch.cuda.stream(stream):
+            stack.enqueue_requests(requests, handle, lanes=lanes)
+        torch.cuda.synchronize(device)
+        status = stack.status()
+        if status:
+            raise RuntimeError(f"device status {status:#x} after warm-up")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            stack.enqueue_requests(requests, handle, lanes=lanes)
+        return g
+
+    # Latency: one lane, requests back to back (each request's own duration).
+    latency_graph = capture(1, 0)
+    # Throughput (the headline): the same requests over the lanes.
+    graph = capture(args.lanes, args.down_splits) if args.lanes > 1 else latency_graph
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             graph.replay()
@@ -563,6 +605,20 @@ def run_ours(args, world, rank, local):
     value = flops_step / (ms_step * 1e-3) / 1e12
     ms_request = ms_step / args.requests
     clk = clocks.summary()
+
+    # Per-request latency: the one-lane graph (heuristic split-K), same requests.
+    latency_ms = ms_request
+    if graph is not latency_graph:
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                latency_graph.replay()
+            s1, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s1.record(stream)
+            for _ in range(max(1, args.steps // 2)):
+                latency_graph.replay()
+            e1.record(stream)
+            e1.synchronize()
+        latency_ms = max_over_ranks(s1.elapsed_time(e1) / max(1, args.steps // 2), world, device) / args.requests
 
     # End to end: pinned host inputs -> device, graph replay, outputs -> host.
     e2e = None
@@ -607,8 +663,9 @@ def run_ours(args, world, rank, local):
         cpu = cpu_baseline(geo, args.cpu_sample_layers)
     baselines = None
     if rank == 0 and world == 1 and not args.no_gpu_baselines:
-        baselines = gpu_baselines(device, geo, weights)
-        baselines["ours_ms_per_request"] = ms_request
+        baselines = gpu_baselines(device, geo, weights, lanes=args.lanes)
+        baselines["ours_ms_per_request"] = latency_ms
+        baselines["ours_lanes_ms_per_request"] = ms_request
         for key in ("torch_native", "reference_cublaslt"):
             if f"{key}_ms_per_request" in baselines:
                 # GEMMs only on both sides (these baselines time no norm / gather / scatter).
@@ -616,13 +673,20 @@ def run_ours(args, world, rank, local):
                                                              baselines["ours_gemms_only_ms_per_request"])
         if "reference_ffn_phase_ms_per_request" in baselines:
             # Whole FFN phase on both sides: norms, gather, GEMMs, scatter, gated residual.
-            baselines["speedup_vs_reference_ffn_phase"] = baselines["reference_ffn_phase_ms_per_request"] / ms_request
+            # Latency: one request at a time on both sides.
+            baselines["speedup_vs_reference_ffn_phase"] = (baselines["reference_ffn_phase_ms_per_request"] /
+                                                           latency_ms)
+        if "reference_ffn_phase_lanes_ms_per_request" in baselines:
+            # Throughput: the same number of concurrent lanes on both sides.
+            baselines["lanes_speedup_vs_reference_ffn_phase"] = (
+                baselines["reference_ffn_phase_lanes_ms_per_request"] / ms_request)
 
     launches = stack.launches_per_request() * args.requests * args.steps
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "ms_per_request": ms_request,
+            "latency_ms_per_request": latency_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
             "config": config_dict(geo, args, world),
@@ -633,6 +697,7 @@ def run_ours(args, world, rank, local):
         }
         print(json.dumps(line), flush=True)
     graph.reset()
+    latency_graph.reset()
     stack.close()
 
 

@@ -256,6 +256,15 @@ int wamffn_block_plan_create(int device, int max_rows, int max_seq, int d_model,
 int wamffn_block_plan_destroy(wamffn_block_plan* plan);
 int wamffn_block_run(wamffn_block_plan* plan, void* stream, const wamffn_block_args* args);
 int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear);
+/* Split-K factor of the down projection for `rows` gathered rows (rows = 0:
+ * every row count up to max_rows); splits = 0 restores the heuristic, which
+ * fills the SMs with feature tiles x splits CTAs.  No counterpart in the
+ * reference (cuBLASLt picks its own split inside Plan::tune,
+ * _cublaslt_inference.cpp:121-174).  A caller that runs several plans
+ * concurrently on one device (independent requests on separate streams)
+ * lowers it: the other lanes fill the SMs, and fewer splits move fewer fp32
+ * partials through L2.  Applies to launches enqueued after the call. */
+int wamffn_block_plan_set_splits(wamffn_block_plan* plan, int rows, int splits);
 /* {up: feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned,
  *  down: same 7 values} for a given row count. */
 int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t* values, int n);

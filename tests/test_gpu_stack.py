@@ -120,3 +120,63 @@ def test_persistent_pass_kernel_equals_three_kernel_stack(cuda_device, tmp_path)
     assert results["0"]["launches"] == 2 * (1 + 3 * 3)
     for key in ("out0", "out1", "hist"):
         assert torch.equal(results["0"][key], results["1"][key]), key
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+def test_lanes_equal_one_lane(cuda_device, splits):
+    """Requests spread over concurrent lanes (own scratch, shared weights,
+    fork / join streams) give the same bits as the same requests in order on
+    one lane with the same down-projection split-K, eagerly and as one graph."""
+    from waminfer_b200.stack import FFNStack, Request, make_weights
+
+    geo = _small_geo(3)
+    weights = make_weights(geo.layers, geo.d, geo.h, cuda_device, seed=9)
+    stack = FFNStack(weights, geo, cuda_device, lanes=3, down_splits=splits)
+    assert all(p.configuration(geo.seq)["down"]["split_k"] == splits for p in stack.plans)
+    reqs = [Request(geo, cuda_device, seed=20 + i) for i in range(5)]
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+
+    stack.enqueue_requests(reqs, stream, lanes=1)
+    torch.cuda.synchronize()
+    ref = [(r.out[0].clone(), r.out[1].clone(), r.history_out.clone()) for r in reqs]
+    for r in reqs:
+        for t in (*r.out, r.history_out):
+            t.zero_()
+    stack.enqueue_requests(reqs, stream)  # 3 lanes
+    torch.cuda.synchronize()
+    for r, (o0, o1, hist) in zip(reqs, ref):
+        assert torch.equal(r.out[0], o0) and torch.equal(r.out[1], o1) and torch.equal(r.history_out, hist)
+
+    side = torch.cuda.Stream(cuda_device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        stack.enqueue_requests(reqs, side.cuda_stream)
+    for r in reqs:
+        for t in (*r.out, r.history_out):
+            t.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    for r, (o0, o1, hist) in zip(reqs, ref):
+        assert torch.equal(r.out[0], o0) and torch.equal(r.out[1], o1) and torch.equal(r.history_out, hist)
+    assert stack.status() == 0
+    graph.reset()
+    stack.close()
+
+
+def test_set_splits_validation(cuda_device):
+    from waminfer_b200 import _lib
+    from waminfer_b200.blocks import BlockPlan
+
+    plan = BlockPlan(cuda_device, 392, 392, 3072, 14336)
+    heuristic = plan.configuration(304)["down"]["split_k"]
+    plan.set_splits(304, 2)
+    assert plan.configuration(304)["down"]["split_k"] == 2
+    assert plan.configuration(392)["down"]["split_k"] == heuristic  # other row counts untouched
+    plan.set_splits(0, 4)
+    assert plan.configuration(392)["down"]["split_k"] == 4
+    plan.set_splits(0, 0)
+    assert plan.configuration(304)["down"]["split_k"] == heuristic
+    for rows, splits in ((393, 2), (-1, 2), (304, 17), (304, -1)):
+        with pytest.raises(_lib.WamffnError, match="outside"):
+            plan.set_splits(rows, splits)
+    plan.close()

@@ -74,6 +74,12 @@ class BlockPlan:
         names = ("feature_tile", "token_pad", "mma_count", "stages", "split_k", "tmem_columns", "tuned")
         return {"up": dict(zip(names, values[:7])), "down": dict(zip(names, values[7:]))}
 
+    def set_splits(self, rows: int, splits: int) -> None:
+        """Down-projection split-K factor for `rows` gathered rows (0: all row
+        counts); 0 restores the SM-filling heuristic.  Lanes of concurrent
+        requests run with fewer splits (``FFNStack(lanes=...)``)."""
+        _lib.check(_lib.lib().wamffn_block_plan_set_splits(self.handle, rows, splits))
+
     def status(self, clear: bool = True) -> int:
         """Device status word (timeout / bad-index bits); synchronises the device."""
         value = ctypes.c_uint32()

@@ -1237,6 +1237,21 @@ int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear) {
   return WAMFFN_OK;
 }
 
+int wamffn_block_plan_set_splits(wamffn_block_plan* plan, int rows, int splits) {
+  if (!plan) return fail(WAMFFN_ERR_INVALID, "null plan");
+  if (rows < 0 || rows > plan->max_rows)
+    return fail(WAMFFN_ERR_INVALID, "rows=%d outside [0, %d]", rows, plan->max_rows);
+  if (splits < 0 || splits > plan->max_splits || splits > plan->h / kBlockK)
+    return fail(WAMFFN_ERR_INVALID, "splits=%d outside [0, %d]", splits,
+                plan->max_splits < plan->h / kBlockK ? plan->max_splits : plan->h / kBlockK);
+  if (rows > 0) {
+    plan->split_override[rows] = splits;
+  } else {
+    for (int r = 1; r <= plan->max_rows; ++r) plan->split_override[r] = splits;
+  }
+  return WAMFFN_OK;
+}
+
 int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t* values, int n) {
   if (!plan || !values) return fail(WAMFFN_ERR_INVALID, "null argument");
   GemmConfig up, down;

@@ -17,6 +17,15 @@ layer-boundary kernel per layer (split-K reduction, history scatter, gated
 residual, next layer's norm + gather).  Everything a request touches is
 preallocated, so a request (or a batch of them) can be captured into one
 CUDA graph.
+
+Lanes: requests share nothing but the weights, so ``FFNStack(lanes=k)`` runs a
+batch of requests on k streams forked from the caller's stream (one block plan,
+i.e. one set of scratch buffers, per lane; the packed weights are shared) and
+joins them back.  The hardware then schedules CTAs of different requests'
+kernels side by side: SMs the up projection leaves idle (56 UMMA pairs on 148
+SMs), the layer-boundary kernels and the launch ramps are filled by the other
+lanes.  Each request's own launches keep their order and their results are
+bit-identical to a single lane with the same split-K factor.
 """
 
 from __future__ import annotations
@@ -111,15 +120,23 @@ class Request:
 class FFNStack:
     """L fused FFN blocks over resident weights on one device."""
 
-    def __init__(self, weights: list[LayerWeights], geo: Geometry, device, eps: float = 1e-6):
+    def __init__(self, weights: list[LayerWeights], geo: Geometry, device, eps: float = 1e-6, lanes: int = 1,
+                 down_splits: int | None = None):
         from waminfer_b200.ffn import pack_weight
 
+        if lanes < 1:
+            raise ValueError("lanes must be at least 1")
         self.weights, self.geo, self.device, self.eps = weights, geo, torch.device(device), eps
         # Tile-packed copies streamed by the GEMMs (one contiguous 16 KB block per tile).
         self.packed = [(pack_weight(w.w_up), pack_weight(w.w_down)) for w in weights]
         # d_hidden from the weights: a tensor-parallel rank holds h / world columns.
-        self.plan = BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d,
-                              d_hidden=weights[0].w_up.shape[0])
+        self.plans = [BlockPlan(self.device, max_rows=geo.seq, max_seq=geo.seq, d_model=geo.d,
+                                d_hidden=weights[0].w_up.shape[0]) for _ in range(lanes)]
+        self.plan = self.plans[0]
+        if down_splits is not None:
+            for plan in self.plans:
+                plan.set_splits(0, down_splits)
+        self._streams = [torch.cuda.Stream(self.device) for _ in range(lanes)] if lanes > 1 else []
         self._pingpong = [torch.empty(geo.seq, geo.d, device=device, dtype=torch.bfloat16) for _ in range(2)]
         self._keep = []  # argument structs referenced by enqueued launches
         self._layer_array = (_lib.LayerWeights * len(weights))()
@@ -175,12 +192,14 @@ class FFNStack:
         self._keep.append(a)
         return a
 
-    def enqueue_pass(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
+    def enqueue_pass(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None,
+                     plan: BlockPlan | None = None) -> None:
         """Runs the L layers with one ``wamffn_stack_run`` (fused layer
         boundaries); with `reuse`, layers 1.. gather its indices and read /
-        write its history."""
+        write its history.  `plan` picks a lane's scratch (default: lane 0)."""
         a = self._stack_args(x_in, x_final, time, reuse)
-        _lib.check(_lib.lib().wamffn_stack_run(self.plan.handle, stream, ctypes.byref(a)))
+        plan = self.plan if plan is None else plan
+        _lib.check(_lib.lib().wamffn_stack_run(plan.handle, stream, ctypes.byref(a)))
 
     def enqueue_pass_blocks(self, x_in, x_final, time, stream: int, reuse: "Request | None" = None) -> None:
         """Same pass as ``enqueue_pass`` with one ``wamffn_block_run`` per layer
@@ -198,13 +217,59 @@ class FFNStack:
             _lib.check(_lib.lib().wamffn_block_run(self.plan.handle, stream, ctypes.byref(a)))
             src = dst
 
+    def _enqueue_request(self, req: Request, stream: int, plan: BlockPlan) -> None:
+        self.enqueue_pass(req.x[0], req.out[0], req.time[0], stream, reuse=req, plan=plan)  # update 0, token reuse
+        self.enqueue_pass(req.x[1], req.out[1], req.time[1], stream, plan=plan)             # update 3, full refresh
+
     def enqueue_request(self, req: Request, stream: int) -> None:
         self._keep.clear()
-        self.enqueue_pass(req.x[0], req.out[0], req.time[0], stream, reuse=req)   # update 0, token reuse
-        self.enqueue_pass(req.x[1], req.out[1], req.time[1], stream)              # update 3, full refresh
+        self._enqueue_request(req, stream, self.plan)
+
+    def set_down_splits(self, splits: int) -> None:
+        """Split-K factor of every lane's down projection for launches enqueued
+        from now on (0: the SM-filling heuristic, best for one lane)."""
+        for plan in self.plans:
+            plan.set_splits(0, splits)
+
+    def enqueue_requests(self, requests: list[Request], stream: int, lanes: int | None = None) -> None:
+        """A batch of independent requests.  With one lane they run in order on
+        `stream`; with k lanes (default: all of the stack's) request i runs on
+        lane i mod k, the lanes' streams wait for `stream` first and `stream`
+        waits for every lane at the end, so the batch is one fork / join
+        (capturable into one CUDA graph)."""
+        self._keep.clear()
+        k = len(self.plans) if lanes is None else lanes
+        if k < 1 or k > len(self.plans):
+            raise ValueError(f"lanes={k} outside [1, {len(self.plans)}]")
+        k = min(k, max(1, len(requests)))
+        if k == 1:
+            for req in requests:
+                self._enqueue_request(req, stream, self.plan)
+            return
+        origin = torch.cuda.ExternalStream(stream, device=self.device)
+        fork = torch.cuda.Event()
+        fork.record(origin)
+        lanes = self._streams[:k]
+        for lane in lanes:
+            lane.wait_event(fork)
+        for i, req in enumerate(requests):
+            k = i % len(lanes)
+            self._enqueue_request(req, lanes[k].cuda_stream, self.plans[k])
+        for lane in lanes:
+            join = torch.cuda.Event()
+            join.record(lane)
+            origin.wait_event(join)
+
+    def status(self, clear: bool = True) -> int:
+        """OR of every lane's device status word (synchronises the device)."""
+        value = 0
+        for plan in self.plans:
+            value |= plan.status(clear)
+        return value
 
     def launches_per_request(self) -> int:
         return 2 * (1 + 3 * self.geo.layers)
 
     def close(self):
-        self.plan.close()
+        for plan in self.plans:
+            plan.close()
