@@ -33,6 +33,8 @@
  *                                  WAMInfer/_triton_inference.py:158-161
  *   wamffn_select_tokens        <- select_tokens(state, features)
  *                                  WAMInfer/approximation.py:55-67
+ *   wamffn_rgb_mandatory        <- the RGB change test of TokenReuse.begin
+ *                                  WAMInfer/approximation.py:31-36
  */
 #ifndef WAMFFN_H
 #define WAMFFN_H
@@ -369,6 +371,17 @@ typedef struct wamffn_select_args {
 } wamffn_select_args;
 
 int wamffn_select_tokens(void* stream, const wamffn_select_args* args);
+
+/* ------------------------------------------------------------------------
+ * Mandatory rows of TokenReuse.begin (approximation.py:31-36) for uint8 HWC
+ * observations now / before [height, width, 3]: mandatory[i] = 1 when the
+ * mean |now - before| over patch i (row-major grid_h x grid_w patches of
+ * height/grid_h x width/grid_w pixels, 3 channels) exceeds 5.0, else 0.
+ * Integer sums, one float32 division: the reference's float32 mask exactly.
+ * height and width must divide by the grid (the reference's reshape).
+ * ---------------------------------------------------------------------- */
+int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int height, int width, int grid_h,
+                         int grid_w, void* mandatory);
 
 #ifdef __cplusplus
 }

@@ -50,3 +50,78 @@ def test_select_tokens_random_vs_oracle(cuda_device, count, seed):
     got = select_rows(now.to(cuda_device), before.to(cuda_device), mandatory, count, 392).cpu()
     ref = oreuse.token_indices(now.float().numpy(), before.float().numpy(), mandatory.numpy(), count, 120, 392)
     assert got.tolist() == ref.tolist()
+
+
+def _lat():
+    return dict(latents=torch.zeros(1, 4, 3, 24, 20))
+
+
+def test_rgb_mandatory_device_matches_reference_golden(cuda_device, golden):
+    """TokenReuse.begin with uint8 CUDA observations (device change test,
+    wamffn_rgb_mandatory) gives the reference's masks and counts: the threshold
+    boundary (+4.999999 / +5.0 / +5.000001 / +9 truncated to uint8), a partial
+    patch change, and the reference's small known-answer case."""
+    from waminfer_b200.approximation import TokenReuse
+
+    g = golden("token_reuse.pt")
+    base = g["rgb_base"]
+    for change in (4.999999, 5.0, 5.000001, 9.0):
+        history = TokenReuse((32, 64, 96, 120))
+        _, observation = history.begin(base.to(cuda_device), _lat(), "task", (1, 2, 2))
+        history.commit(observation, torch.empty(1, 120, 1), torch.empty(1, 1, 120, 1))
+        current = (base.double() + change).to(torch.uint8).to(cuda_device)
+        reuse, _ = history.begin(current, _lat(), "task", (1, 2, 2))
+        mask, count = g["rgb_masks"][("uint8", change)]
+        assert torch.equal(reuse["mandatory"].cpu(), mask), change
+        assert reuse["count"] == count, change
+
+    history = TokenReuse((32, 64, 96, 120))
+    _, observation = history.begin(base.to(cuda_device), _lat(), "task", (1, 2, 2))
+    history.commit(observation, torch.empty(1, 120, 1), torch.empty(1, 1, 120, 1))
+    reuse, _ = history.begin(g["patch_change_image"].to(cuda_device), _lat(), "task", (1, 2, 2))
+    assert torch.equal(reuse["mandatory"].cpu(), g["patch_change_mandatory"])
+    assert reuse["count"] == g["patch_change_count"]
+
+    history = TokenReuse((1, 2, 3, 4))
+    inputs = dict(latents=torch.zeros(1, 4, 3, 4, 4))
+    image = torch.zeros(8, 8, 3, dtype=torch.uint8, device=cuda_device)
+    reuse, observation = history.begin(image, inputs, "task", (1, 2, 2))
+    assert reuse["count"] == g["small_first_count"]
+    history.commit(observation, torch.ones(1, 4, 8), torch.ones(1, 1, 4, 8))
+    image[:4, 4:] = 30
+    reuse, _ = history.begin(image, inputs, "task", (1, 2, 2))
+    assert reuse["count"] == g["small_second_count"]
+    assert torch.equal(reuse["mandatory"].cpu(), g["small_second_mandatory"])
+
+
+def test_rgb_mandatory_device_threshold_and_random(cuda_device):
+    """Patch sums of exactly 5 x 3072 - 1, 5 x 3072 and 5 x 3072 + 1 (means
+    just below, at and above the threshold) and random observations against
+    the oracle's float32 numpy test."""
+    import numpy as np
+
+    from waminfer_b200.approximation import TokenReuse
+
+    before = np.zeros((384, 320, 3), dtype=np.uint8)
+    now = np.full((384, 320, 3), 5, dtype=np.uint8)
+    now[0, 0, 0] = 6      # patch 0: 15361 -> mandatory
+    now[0, 32, 0] = 4     # patch 1: 15359 -> not
+    now[32, 0, :] = 0     # patch 10: below
+    now[33, 0, :] = 10    # patch 10: back to exactly 15360 -> not
+    rng = np.random.default_rng(3)
+    cases = [(now, before)]
+    for scale in (3, 8, 12, 40):
+        a = rng.integers(0, 256, (384, 320, 3), dtype=np.uint8)
+        b = np.clip(a.astype(np.int32) + rng.integers(-scale, scale + 1, a.shape), 0, 255).astype(np.uint8)
+        cases.append((a, b))
+    for a, b in cases:
+        got = TokenReuse.mandatory_rows_device(torch.from_numpy(a).to(cuda_device),
+                                               torch.from_numpy(b).to(cuda_device), 12, 10)
+        ref = oreuse.mandatory_mask(a, b, 12, 10)
+        assert got.cpu().numpy().tolist() == ref.tolist()
+    first = TokenReuse.mandatory_rows_device(torch.from_numpy(now).to(cuda_device),
+                                             torch.from_numpy(before).to(cuda_device), 12, 10).cpu()
+    assert first[0] and not first[1] and not first[10]
+    with pytest.raises(ValueError, match="split"):
+        TokenReuse.mandatory_rows_device(torch.zeros(385, 320, 3, dtype=torch.uint8, device=cuda_device),
+                                         torch.zeros(385, 320, 3, dtype=torch.uint8, device=cuda_device), 12, 10)

@@ -2,10 +2,11 @@
 
 Mirror of the reference's ``WAMInfer/approximation.py`` interface:
 
-* ``TokenReuse(buckets)`` with ``capacities``, ``begin`` and ``commit`` -- host
-  logic run once per request: the float32 RGB change test that marks rows
-  mandatory and the refresh count rounded up to a capacity bucket
-  (reference ``:8-52``);
+* ``TokenReuse(buckets)`` with ``capacities``, ``begin`` and ``commit`` -- run
+  once per request: the float32 RGB change test that marks rows mandatory
+  (numpy for host images as in the reference; ``wamffn_rgb_mandatory`` on the
+  device for uint8 CUDA images, bit-identical) and the refresh count rounded
+  up to a capacity bucket (reference ``:8-52``);
 * ``select_tokens(state, features)`` -- the per-request row selection on the
   device (``wamffn_select_tokens``): fp32 relative L1 score against the
   committed first-layer features, mandatory rows first, stable descending
@@ -52,21 +53,52 @@ class TokenReuse:
         patches = diff.reshape(h, rgb.shape[0] // h, w, rgb.shape[1] // w, 3)
         return patches.mean(axis=(1, 3, 4)).reshape(-1) > 5.0
 
+    @staticmethod
+    def mandatory_rows_device(rgb: torch.Tensor, previous: torch.Tensor, h: int, w: int) -> torch.Tensor:
+        """``mandatory_rows`` on the GPU for uint8 HWC images (``wamffn_rgb_mandatory``):
+        integer sums of |change| per patch, one float32 division, ``> 5``."""
+        if rgb.dtype != torch.uint8 or previous.dtype != torch.uint8 or rgb.shape != previous.shape:
+            raise ValueError("device observations must be uint8 HWC images of one shape")
+        if not (rgb.is_cuda and previous.device == rgb.device):
+            raise ValueError("device observations must be on one CUDA device")
+        if rgb.shape[0] % h or rgb.shape[1] % w:
+            raise ValueError(f"a {tuple(rgb.shape)} observation does not split into {h}x{w} patches")
+        rgb, previous = rgb.contiguous(), previous.contiguous()
+        out = torch.empty(h * w, dtype=torch.uint8, device=rgb.device)
+        with torch.cuda.device(rgb.device):
+            _lib.check(_lib.lib().wamffn_rgb_mandatory(torch.cuda.current_stream(rgb.device).cuda_stream,
+                                                       rgb.data_ptr(), previous.data_ptr(), rgb.shape[0],
+                                                       rgb.shape[1], h, w, out.data_ptr()))
+        return out.bool()
+
     def begin(self, image, inputs, prompt, patch):
-        """Plans one request: returns (reuse dict, observation to commit on success)."""
+        """Plans one request: returns (reuse dict, observation to commit on success).
+        A uint8 CUDA tensor observation is tested on the device; anything else
+        (PIL images, numpy arrays) on the host as in the reference."""
         latents = inputs["latents"]
         h, w = latents.shape[-2] // patch[1], latents.shape[-1] // patch[2]
         n = h * w
-        rgb = np.array(image, copy=True)  # own the snapshot: callers recycle camera buffers
+        on_device = isinstance(image, torch.Tensor) and image.is_cuda
+        if on_device:
+            if image.dtype != torch.uint8:
+                raise ValueError("device observations must be uint8 HWC images")
+            rgb = image.detach().clone()  # own the snapshot: callers recycle camera buffers
+        else:
+            rgb = np.array(image, copy=True)
         if rgb.ndim != 3 or rgb.shape[-1] != 3 or latents.shape[2] < 2:
             raise ValueError("Token reuse requires one HWC RGB observation and future video frames")
-        key = (prompt, tuple(latents.shape), rgb.shape)
+        key = (prompt, tuple(latents.shape), tuple(rgb.shape))
         if key != self.key:
             self.reset()
         if self.image is None:
             mandatory = np.ones(n, dtype=bool)
+        elif on_device and (isinstance(self.image, torch.Tensor) or self.image.dtype == np.uint8):
+            previous = self.image if isinstance(self.image, torch.Tensor) else torch.from_numpy(self.image)
+            mandatory = self.mandatory_rows_device(rgb, previous.to(rgb.device), h, w)
         else:
-            mandatory = self.mandatory_rows(rgb, self.image, h, w)
+            host = rgb.cpu().numpy() if on_device else rgb
+            previous = self.image.cpu().numpy() if isinstance(self.image, torch.Tensor) else self.image
+            mandatory = self.mandatory_rows(host, previous, h, w)
         required = int(mandatory.sum())
         required += math.ceil(0.25 * (n - required))
         count = next(b for b in self.capacities(n) if b >= required)

@@ -1330,4 +1330,29 @@ int wamffn_select_tokens(void* stream, const wamffn_select_args* a) {
   return WAMFFN_OK;
 }
 
+int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int height, int width, int grid_h,
+                         int grid_w, void* mandatory) {
+  if (!now || !before || !mandatory) return fail(WAMFFN_ERR_INVALID, "null pointer");
+  if (height < 1 || width < 1 || grid_h < 1 || grid_w < 1)
+    return fail(WAMFFN_ERR_INVALID, "sizes must be positive");
+  if (height % grid_h || width % grid_w)
+    return fail(WAMFFN_ERR_INVALID, "a %dx%d image does not split into %dx%d patches", height, width, grid_h, grid_w);
+  const long long patch_values = (long long)(height / grid_h) * (width / grid_w) * 3;
+  if (patch_values * 255 >= (1ll << 24))
+    return fail(WAMFFN_ERR_UNSUPPORTED, "patches of %lld values exceed the exact float32 sum range", patch_values);
+  if ((long long)grid_h * grid_w > 65535) return fail(WAMFFN_ERR_UNSUPPORTED, "more than 65535 patches");
+  RgbParams p{};
+  p.now = static_cast<const unsigned char*>(now);
+  p.before = static_cast<const unsigned char*>(before);
+  p.width = width;
+  p.ph = height / grid_h;
+  p.pw = width / grid_w;
+  p.grid_w = grid_w;
+  p.mandatory = static_cast<unsigned char*>(mandatory);
+  rgb_mandatory_kernel<<<grid_h * grid_w, kRgbThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  WAMFFN_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
 }  // extern "C"

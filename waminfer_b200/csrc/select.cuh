@@ -86,4 +86,46 @@ __global__ void __launch_bounds__(kSelectThreads) select_tokens_kernel(const Sel
   if (tid == 0) pdl_launch_dependents();
 }
 
+// Mandatory rows of TokenReuse.begin (WAMInfer/approximation.py:31-36) for
+// uint8 HWC observations: row i (patch (i / grid_w, i % grid_w) of
+// ph x pw pixels) is mandatory when the float32 mean of |now - before| over
+// its ph x pw x 3 values exceeds 5.  For uint8 inputs every |difference| is an
+// integer, so the float32 sum the reference accumulates is exact in any order
+// (ph * pw * 3 * 255 < 2^24); the kernel sums integers and divides once, as
+// numpy's mean does, which gives the reference's mask bit for bit.
+constexpr int kRgbThreads = 256;
+
+struct RgbParams {
+  const unsigned char* now;     // [height, width, 3]
+  const unsigned char* before;  // [height, width, 3]
+  int width;
+  int ph, pw;                   // patch height / width in pixels
+  int grid_w;
+  unsigned char* mandatory;     // [grid_h * grid_w]
+};
+
+__global__ void __launch_bounds__(kRgbThreads) rgb_mandatory_kernel(const RgbParams p) {
+  __shared__ int partial[kRgbThreads / 32];
+  const int patch = blockIdx.x;
+  const int py = patch / p.grid_w, px = patch % p.grid_w;
+  const int row_bytes = p.pw * 3;
+  const int total = p.ph * row_bytes;
+  const size_t base = (size_t(py) * p.ph * p.width + size_t(px) * p.pw) * 3;
+  int sum = 0;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int r = i / row_bytes, c = i - r * row_bytes;
+    const size_t off = base + size_t(r) * p.width * 3 + c;
+    sum += abs(int(p.now[off]) - int(p.before[off]));
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < kRgbThreads / 32; ++w) s += partial[w];
+    const float mean = __fdiv_rn(float(s), float(total));
+    p.mandatory[patch] = mean > 5.0f ? 1 : 0;
+  }
+}
+
 }  // namespace wamffn
