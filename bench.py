@@ -37,8 +37,8 @@ METRIC = "FFN-stack ms/request and TFLOP/s (2F, 32/120 reuse) at 1/2/4/8 B200; %
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram__bytes_read.sum + dram__bytes_write.sum of one up-projection launch at
 # M = 392 from the committed ncu capture (profiles/umma_gemm_ffn_m392.md):
-# 90.56 MB read + 2.95 MB written.
-UP_GEMM_DRAM_BYTES = 93_512_000
+# 90.57 MB read + 3.86 MB written.
+UP_GEMM_DRAM_BYTES = 94_424_832
 
 
 def parse():
