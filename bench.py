@@ -623,19 +623,19 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.Stream(device)
     handle = stream.cuda_stream
 
-    def capture(lanes, splits):
+    def capture(lanes, splits, reqs=requests):
         # Eager warm-up (also checks the device status words), then capture the
         # R requests over `lanes` lanes into one graph.
         stack.set_down_splits(splits)
         with torch.cuda.stream(stream):
-            stack.enqueue_requests(requests, handle, lanes=lanes)
+            stack.enqueue_requests(reqs, handle, lanes=lanes)
         torch.cuda.synchronize(device)
         status = stack.status()
         if status:
             raise RuntimeError(f"device status {status:#x} after warm-up")
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            stack.enqueue_requests(requests, handle, lanes=lanes)
+            stack.enqueue_requests(reqs, handle, lanes=lanes)
         return g
 
     # Latency: one lane, requests back to back (each request's own duration).
@@ -684,39 +684,75 @@ def run_ours(args, world, rank, local):
             e1.synchronize()
         latency_ms = max_over_ranks(s1.elapsed_time(e1) / max(1, args.steps // 2), world, device) / args.requests
 
-    # End to end: pinned host inputs -> device, graph replay, outputs -> host.
+    # End to end: every step copies its R requests' inputs from pinned host
+    # memory and its outputs back, around the same lanes graph.  Two sets of
+    # request buffers alternate between steps so that the copies of one step
+    # overlap the compute of its neighbours (a serving loop's double
+    # buffering): inputs of step k go up on a copy stream while step k-1
+    # computes, outputs of step k come down while step k+1 computes.  The
+    # timed region runs from before the first input copy to after the last
+    # output copy.
     e2e = None
     if not args.no_e2e:
+        sets = [(requests, graph)]
+        if args.steps > 1:
+            other = [Request(geo, device, seed=rank * 100_000 + args.requests + i) for i in range(args.requests)]
+            sets.append((other, capture(args.lanes, args.down_splits if args.lanes > 1 else 0, other)))
         host_in = [[r.x[0].cpu().pin_memory(), r.x[1].cpu().pin_memory(), r.indices.cpu().pin_memory()]
                    for r in requests]
-        host_out = [[torch.empty_like(r.out[0], device="cpu").pin_memory() for _ in range(2)] for r in requests]
+        host_out = [[[torch.empty_like(r.out[0], device="cpu").pin_memory() for _ in range(2)] for r in reqs]
+                    for reqs, _ in sets]
         h2d = sum(t.numel() * t.element_size() for hs in host_in for t in hs)
-        d2h = sum(t.numel() * t.element_size() for hs in host_out for t in hs)
+        d2h = sum(t.numel() * t.element_size() for hs in host_out[0] for t in hs)
+        copy_in, copy_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        inputs_ready = [torch.cuda.Event() for _ in sets]
+        computed = [torch.cuda.Event() for _ in sets]
+        outputs_copied = [torch.cuda.Event() for _ in sets]
 
-        def e2e_step():
-            with torch.cuda.stream(stream):
-                for r, hi in zip(requests, host_in):
-                    r.x[0].copy_(hi[0], non_blocking=True)
-                    r.x[1].copy_(hi[1], non_blocking=True)
-                    r.indices.copy_(hi[2], non_blocking=True)
-                graph.replay()
-                for r, ho in zip(requests, host_out):
-                    ho[0].copy_(r.out[0], non_blocking=True)
-                    ho[1].copy_(r.out[1], non_blocking=True)
+        def e2e_run(steps):
+            begin = torch.cuda.Event()
+            begin.record(stream)
+            copy_in.wait_event(begin)
+            for k in range(steps):
+                j = k % len(sets)
+                reqs, g = sets[j]
+                with torch.cuda.stream(copy_in):
+                    copy_in.wait_event(computed[j])       # the set's previous graph has read its inputs
+                    for r, hi in zip(reqs, host_in):
+                        r.x[0].copy_(hi[0], non_blocking=True)
+                        r.x[1].copy_(hi[1], non_blocking=True)
+                        r.indices.copy_(hi[2], non_blocking=True)
+                    inputs_ready[j].record(copy_in)
+                stream.wait_event(inputs_ready[j])
+                stream.wait_event(outputs_copied[j])     # the set's previous outputs are on the host
+                with torch.cuda.stream(stream):
+                    g.replay()
+                computed[j].record(stream)
+                with torch.cuda.stream(copy_out):
+                    copy_out.wait_event(computed[j])
+                    for r, ho in zip(reqs, host_out[j]):
+                        ho[0].copy_(r.out[0], non_blocking=True)
+                        ho[1].copy_(r.out[1], non_blocking=True)
+                    outputs_copied[j].record(copy_out)
+            for ev in outputs_copied:
+                stream.wait_event(ev)
 
-        e2e_step()
+        e2e_run(len(sets))
         torch.cuda.synchronize(device)
         barrier(world)
         s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s2.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         e2.record(stream)
         e2.synchronize()
         barrier(world)
         ms_e2e = max_over_ranks(s2.elapsed_time(e2) / args.steps, world, device)
         e2e = {"value": flops_step / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
-               "ms_per_request": ms_e2e / args.requests, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+               "ms_per_request": ms_e2e / args.requests, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "copies": "double-buffered: a step's copies overlap its neighbours' compute" if len(sets) > 1
+               else "serial"}
+        for _, g in sets[1:]:
+            g.reset()
 
     roof = time_dominant_kernel(device, geo, pk)
     roof["peak_kind"] = f"{pk_kind} (burst bf16 GEMM)"
