@@ -283,6 +283,12 @@ int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t
  * history scatter, gated residual and the next layer's norm + gather run as
  * one kernel.  No attention runs between the FFNs: every layer's norm input
  * is the previous layer's residual (update = NULL).
+ * With the environment variable WAMFFN_PASS=1 a pass is one persistent
+ * launch instead, whose CTAs (one per SM) synchronise through grid-wide
+ * counters: it needs the whole device, so such passes must not run
+ * concurrently with other work (several block plans on several streams);
+ * a pass whose CTAs cannot all become resident ends with WAMFFN_DEV_TIMEOUT
+ * in the status word.
  * ---------------------------------------------------------------------- */
 typedef struct wamffn_layer_weights {
   const void* w_up;     /* [h, d] or packed */

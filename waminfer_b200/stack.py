@@ -31,6 +31,7 @@ bit-identical to a single lane with the same split-K factor.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass
 
 import torch
@@ -126,6 +127,10 @@ class FFNStack:
 
         if lanes < 1:
             raise ValueError("lanes must be at least 1")
+        pass_flag = os.environ.get("WAMFFN_PASS", "")
+        if lanes > 1 and pass_flag and pass_flag[0] not in "0nNfF":  # the library's reading of the flag
+            # The persistent pass kernel's grid barriers need every SM: lanes would starve each other.
+            raise ValueError("WAMFFN_PASS=1 (one persistent launch per pass) cannot run in concurrent lanes")
         self.weights, self.geo, self.device, self.eps = weights, geo, torch.device(device), eps
         # Tile-packed copies streamed by the GEMMs (one contiguous 16 KB block per tile).
         self.packed = [(pack_weight(w.w_up), pack_weight(w.w_down)) for w in weights]
