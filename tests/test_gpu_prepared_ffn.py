@@ -59,6 +59,9 @@ def test_prepared_ffn_contract(cuda_device):
         assert not torch.equal(updated, actual)
         torch.testing.assert_close(updated, ffn(x), atol=0.01, rtol=0.04)
         assert not first.prepare((16,))
+        # An empty input is an unprepared row count: the native FFN, like the reference.
+        empty = torch.empty(1, 0, 128, device=cuda_device, dtype=torch.bfloat16)
+        assert first.forward(0, empty).shape == (1, 0, 128)
         first.close()
         assert set(_PLANS) == before | set(second.keys.values())
     finally:
