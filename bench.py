@@ -258,12 +258,15 @@ def time_dominant_kernel(device, geo, pk):
                 plan.run(x, ws[i % 4], b)
         graph.replay()
         torch.cuda.synchronize(device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        graph.replay()
-        end.record(stream)
-        end.synchronize()
-    ms = start.elapsed_time(end) / iters
+        samples = []
+        for _ in range(3):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            graph.replay()
+            end.record(stream)
+            end.synchronize()
+            samples.append(start.elapsed_time(end) / iters)
+    ms = statistics.median(samples)
     graph.reset()
     flops = 2 * m * geo.d * geo.h
     achieved = flops / (ms * 1e-3) / 1e12
@@ -622,6 +625,10 @@ def run_ours(args, world, rank, local):
     requests = [Request(geo, device, seed=rank * 100_000 + i) for i in range(args.requests)]
     stream = torch.cuda.Stream(device)
     handle = stream.cuda_stream
+    # The dominant kernel alone, first: against the burst peak it needs the
+    # clocks of a GPU that is not yet running into its power cap.
+    roof = time_dominant_kernel(device, geo, pk)
+    roof["peak_kind"] = f"{pk_kind} (burst bf16 GEMM)"
 
     def capture(lanes, splits, reqs=requests):
         # Eager warm-up (also checks the device status words), then capture the
@@ -783,8 +790,6 @@ def run_ours(args, world, rank, local):
         for _, g in sets[1:]:
             g.reset()
 
-    roof = time_dominant_kernel(device, geo, pk)
-    roof["peak_kind"] = f"{pk_kind} (burst bf16 GEMM)"
     roof_ms = request_roofline_ms(geo, pk)
 
     cpu = None
