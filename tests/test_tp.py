@@ -138,3 +138,51 @@ def test_tp_stack_on_two_gpus_matches_one_gpu(cuda_device, tmp_path):
     kept = sorted(set(range(geo.current)) - set(req.indices[: geo.count].tolist()))
     assert torch.equal(outs[0]["hist"][:, kept], req.history_in[:, kept].cpu())
     stack.close()
+
+
+@pytest.mark.gpu
+def test_tp_entry_point_identity_and_failing_reduction(cuda_device):
+    """wamffn_stack_run_tp on one GPU: with an identity reduction hook the
+    pass equals wamffn_stack_run bit for bit (the rank's split sum is the
+    boundary's own split-order sum); a hook that fails at layer 1 stops the
+    enqueue with the hook's status and a message, and the plan keeps working."""
+    import ctypes
+
+    from waminfer_b200 import _lib
+    from waminfer_b200.stack import FFNStack, Geometry, Request, make_weights
+
+    geo = Geometry(layers=3)
+    stack = FFNStack(make_weights(geo.layers, geo.d, geo.h, cuda_device, seed=23), geo, cuda_device)
+    req = Request(geo, cuda_device, seed=24)
+    s = torch.cuda.current_stream(cuda_device).cuda_stream
+    reduce = torch.empty(geo.seq, geo.d, dtype=torch.float32, device=cuda_device)
+    calls = []
+
+    def hook(fail_at):
+        def fn(user, buffer, count, stream):
+            calls.append(count)
+            return 5 if len(calls) - 1 == fail_at else 0
+        return _lib.ALLREDUCE_FN(fn)
+
+    expected = torch.empty_like(req.out[0])
+    stack.enqueue_pass(req.x[0], expected, req.time[0], s, reuse=req)
+    identity = hook(-1)
+    args = stack._stack_args(req.x[0], req.out[0], req.time[0], req)
+    assert _lib.lib().wamffn_stack_run_tp(stack.plan.handle, s, ctypes.byref(args), reduce.data_ptr(), identity,
+                                          None) == 0
+    torch.cuda.synchronize()
+    assert len(calls) == geo.layers and calls[0] == geo.seq * geo.d and calls[1] == req.indices.numel() * geo.d
+    assert torch.equal(req.out[0], expected)
+
+    calls.clear()
+    failing = hook(1)
+    args = stack._stack_args(req.x[0], req.out[0], req.time[0], req)
+    status = _lib.lib().wamffn_stack_run_tp(stack.plan.handle, s, ctypes.byref(args), reduce.data_ptr(), failing,
+                                            None)
+    assert status == 5 and len(calls) == 2
+    assert "allreduce callback failed at layer 1" in _lib.lib().wamffn_last_error().decode()
+    torch.cuda.synchronize()
+    stack.enqueue_pass(req.x[1], req.out[1], req.time[1], s)
+    torch.cuda.synchronize()
+    assert stack.status() == 0
+    stack.close()
