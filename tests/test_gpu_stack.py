@@ -44,11 +44,14 @@ def test_stack_equals_chained_blocks(cuda_device):
     stack.close()
 
 
-def test_stack_follows_oracle_with_reuse(cuda_device):
-    from waminfer_b200.stack import FFNStack, Request, make_weights
+@pytest.mark.parametrize("count", [32, 64, 96])
+def test_stack_follows_oracle_with_reuse(cuda_device, count):
+    """Capacity buckets of BASELINE config 2 (16 and 32 refreshed rows both use
+    the 32 bucket; 64; 96): 304, 336 and 368 gathered rows."""
+    from waminfer_b200.stack import FFNStack, Geometry, Request, make_weights
 
     torch.backends.cuda.matmul.allow_tf32 = False
-    geo = _small_geo(3)
+    geo = Geometry(layers=3, count=count)
     weights = make_weights(geo.layers, geo.d, geo.h, cuda_device, seed=4)
     stack = FFNStack(weights, geo, cuda_device)
     req = Request(geo, cuda_device, seed=6)
