@@ -254,15 +254,15 @@ class FFNStack:
         origin = torch.cuda.ExternalStream(stream, device=self.device)
         fork = torch.cuda.Event()
         fork.record(origin)
-        lanes = self._streams[:k]
-        for lane in lanes:
-            lane.wait_event(fork)
+        lane_streams = self._streams[:k]
+        for lane_stream in lane_streams:
+            lane_stream.wait_event(fork)
         for i, req in enumerate(requests):
-            k = i % len(lanes)
-            self._enqueue_request(req, lanes[k].cuda_stream, self.plans[k])
-        for lane in lanes:
+            j = i % k
+            self._enqueue_request(req, lane_streams[j].cuda_stream, self.plans[j])
+        for lane_stream in lane_streams:
             join = torch.cuda.Event()
-            join.record(lane)
+            join.record(lane_stream)
             origin.wait_event(join)
 
     def status(self, clear: bool = True) -> int:
