@@ -104,6 +104,29 @@ def test_down_projection_split_k(cuda_device, weights, packed, rows, layout):
     plan.close()
 
 
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("rows,n_out,k_in", [(1, 384, 256), (100, 384, 1024), (300, 640, 512), (512, 128, 3072)])
+def test_single_cta_tiles(cuda_device, rows, n_out, k_in, gelu):
+    """An odd number of 128-feature tiles runs one CTA per tile (no UMMA pair),
+    with one UMMA up to 256 rows and two above (rows 300, 512); with and
+    without tuned split-K, against the fp32 oracle."""
+    from waminfer_b200.ffn import Plan, pack_weight
+
+    g = torch.Generator(device=cuda_device).manual_seed(rows + n_out + k_in)
+    x = randn((rows, k_in), cuda_device, g)
+    w = (torch.randn(n_out, k_in, device=cuda_device, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(n_out, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    pre = x.float() @ w.float().T + bias.float()
+    ref = offn.bf16(offn.gelu_tanh(pre) if gelu else pre)
+    for weight in (w, pack_weight(w)):
+        for exhaustive in (False, True):
+            plan = Plan(x, weight, bias, exhaustive=exhaustive, gelu=gelu)
+            assert plan.selected_configuration()[0] == 128  # one CTA per 128-feature tile
+            close(plan.run(x, weight, bias), ref)
+            assert plan.status() == 0
+            plan.close()
+
+
 def _block_inputs(cuda_device, weights, seq, per_token=True):
     g = weights["gen"]
     x = randn((1, seq, D), cuda_device, g)
