@@ -88,8 +88,10 @@ def test_stack_follows_oracle_with_reuse(cuda_device, count):
 
 def test_persistent_pass_kernel_equals_three_kernel_stack(cuda_device, tmp_path):
     """The opt-in persistent pass kernel (WAMFFN_PASS=1, one launch per pass)
-    computes the same bits as the default three-kernel stack; the variable is
-    read once per process, so each variant runs in its own interpreter."""
+    computes the same bits as the default three-kernel stack, and the stack
+    without UMMA pairs (WAMFFN_PAIR=0) agrees within the stack tolerance; the
+    variables are read once per process, so each variant runs in its own
+    interpreter."""
     import os
     import subprocess
     import sys
@@ -123,6 +125,16 @@ def test_persistent_pass_kernel_equals_three_kernel_stack(cuda_device, tmp_path)
     assert results["0"]["launches"] == 2 * (1 + 3 * 3)
     for key in ("out0", "out1", "hist"):
         assert torch.equal(results["0"][key], results["1"][key]), key
+
+    # The same stack with one CTA per 128-feature tile (WAMFFN_PAIR=0, no UMMA
+    # pairs): the same sums per element, within the stack tolerance.
+    env = dict(os.environ, WAMFFN_PASS="0", WAMFFN_PAIR="0", PYTHONPATH=root)
+    out = tmp_path / "nopair.pt"
+    subprocess.run([sys.executable, str(script), str(out)], check=True, env=env, cwd=root, timeout=600)
+    single = torch.load(out)
+    for key in ("out0", "out1", "hist"):
+        ok, msg = offn.check_close(single[key], results["0"][key].float(), max_abs=6e-2)
+        assert ok, f"{key}: {msg}"
 
 
 @pytest.mark.parametrize("splits", [1, 3])
