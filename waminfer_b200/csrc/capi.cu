@@ -1146,12 +1146,16 @@ int stack_run_impl(wamffn_block_plan* plan, void* stream_, const wamffn_stack_ar
     rc = launch_gemm(up, EPI_GELU_BF16, stream, w.w_up, a->weights_packed != 0, plan->gathered, w.b_up, plan->hidden,
                      plan->status, pdl);
     if (rc) return rc;
-    rc = launch_gemm(down, EPI_PARTIAL_F32, stream, w.w_down, a->weights_packed != 0, plan->hidden, nullptr,
-                     plan->partial, plan->status, pdl);
+    // Unsplit K (concurrent lanes): the GEMM applies the bias and rounds to
+    // bf16 itself, the boundary reads half the bytes.  Same values either way.
+    const bool direct = !tp && down.splits == 1;
+    rc = launch_gemm(down, direct ? EPI_BIAS_BF16 : EPI_PARTIAL_F32, stream, w.w_down, a->weights_packed != 0,
+                     plan->hidden, direct ? w.b_down : nullptr, plan->partial, plan->status, pdl);
     if (rc) return rc;
     BoundaryParams b{};
     b.partial = plan->partial;
     b.splits = down.splits;
+    b.out_bf16 = direct ? 1 : 0;
     if (tp) {
       // This rank's share of the down projection, summed over its splits,
       // then over the ranks; the boundary reads the one reduced sum.
@@ -1208,7 +1212,8 @@ int stack_run_impl(wamffn_block_plan* plan, void* stream_, const wamffn_stack_ar
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, boundary_kernel, b));
+    if (b.out_bf16) WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, boundary_kernel<true>, b));
+    else WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, boundary_kernel<false>, b));
     g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   return WAMFFN_OK;

@@ -357,6 +357,7 @@ struct BoundaryParams {
   __nv_bfloat16* x_final;       // [seq, dim], written after the last layer
   float eps;
   unsigned int* status;
+  int out_bf16;                 // 1: `partial` holds bf16 [m, dim] outputs with the bias applied (unsplit K)
 };
 
 // Sum of the split-K partials of one rank's down projection, in split order
@@ -385,6 +386,9 @@ constexpr int kBoundarySplitsBatch = 2;  // split-K partials loaded per batch of
 // the grid-dependency wait; after it the residual row, the gate, the bias and
 // the partials are read in batches of independent loads.  Registers are capped so that three CTAs (three rows)
 // stay resident per SM.
+// kOutBf16: the down projection ran unsplit and stored bf16(acc + bias) itself
+// (p.out_bf16); a separate instantiation keeps the split-K path's registers.
+template <bool kOutBf16>
 __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const BoundaryParams p) {
   extern __shared__ float xrow[];
   __shared__ float red[32];
@@ -467,7 +471,9 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
     const uint4 y_packed = *reinterpret_cast<const uint4*>(p.y + size_t(row) * p.dim + e);
     const uint4 g_packed = modulation8_packed(p.mod, p.time, p.ts, row, 5, p.dim, e);
     float o[8];
-    if (j >= 0) {
+    if (kOutBf16 && j >= 0) {
+      load8(reinterpret_cast<const __nv_bfloat16*>(p.partial) + size_t(j) * p.dim + e, o);
+    } else if (j >= 0) {
       const float* base = p.partial + size_t(j) * p.dim + e;
       const size_t split_stride = size_t(p.m) * p.dim;
       float acc[8];
