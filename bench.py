@@ -468,6 +468,50 @@ def reference_ffn_phase_ms(device, geo, weights, replays, lanes=1, ours_latency=
     return out
 
 
+def norm_timings(device, geo, replays):
+    """The modulated norm at S = 392 with per-token time rows,
+    CROSS_RESIDUAL and FFN_RESIDUAL modes: this library's op against the
+    reference's Triton kernel (baseline/_ref, imported through the stub parent
+    package), 30 distinct inputs per replay so that each call reads its rows
+    from HBM."""
+    import types
+
+    from waminfer_b200.norm import modulated_norm
+
+    ref_root = ROOT / "baseline" / "_ref"
+    if "WAMInfer" not in sys.modules:
+        pkg = types.ModuleType("WAMInfer")
+        pkg.__path__ = [str(ref_root / "WAMInfer")]
+        sys.modules["WAMInfer"] = pkg
+    from WAMInfer import _triton_inference as rt
+
+    g = torch.Generator(device=device).manual_seed(5)
+    s, d, n = geo.seq, geo.d, 30
+
+    def rnd(*shape, std=1.0):
+        return (torch.randn(*shape, device=device, generator=g) * std).to(torch.bfloat16)
+
+    xs = [rnd(1, s, d) for _ in range(n)]
+    ups = [rnd(1, s, d) for _ in range(n)]
+    times = [rnd(1, s, 6, d, std=0.1) for _ in range(n)]
+    mod, prev = rnd(1, 6, d, std=0.1), rnd(1, 6, d, std=0.1)
+    out = {}
+    for name, mode, previous in (("cross_residual", rt.CROSS_RESIDUAL, None), ("ffn_residual", rt.FFN_RESIDUAL, prev)):
+        def ours():
+            for x, u, t in zip(xs, ups, times):
+                modulated_norm(x, u, mod, previous, t, None, None, mode, 1e-6)
+
+        def reference():
+            for x, u, t in zip(xs, ups, times):
+                rt.modulated_norm(x, u, mod, previous, t, None, None, mode, 1e-6)
+
+        with torch.no_grad():
+            t_ours = _graph_ms_per_replay(ours, device, replays) / n * 1e3
+            t_ref = _graph_ms_per_replay(reference, device, replays) / n * 1e3
+        out[name] = {"ours_us": t_ours, "reference_triton_us": t_ref, "speedup": t_ref / t_ours}
+    return out
+
+
 def projection_timings(device, geo, replays):
     """Attention-side projections of one block at M = 392 rows (packed QKV
     3072 -> 9216, self-attention output, cross-attention query and output,
@@ -552,6 +596,10 @@ def gpu_baselines(device, geo, weights, replays=5, lanes=1, ours_latency=None, o
         out["projections_m392"] = projection_timings(device, geo, replays)
     except Exception as exc:  # reported, not fatal
         out["projections_error"] = f"{type(exc).__name__}: {exc}"
+    try:
+        out["modulated_norm_s392"] = norm_timings(device, geo, replays)
+    except Exception as exc:  # reported, not fatal
+        out["modulated_norm_error"] = f"{type(exc).__name__}: {exc}"
     for up, down in our_plans.values():
         up.close()
         down.close()
