@@ -78,25 +78,40 @@ class Clocks:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuid: str | None):
+    def __init__(self, uuid: str | None, enabled: bool = True):
         self.uuid = uuid
+        self.enabled = enabled  # only the rank that prints the line samples (one nvidia-smi per box)
         self.proc = None
         self.file = None
 
     def __enter__(self):
+        if not self.enabled:
+            return self
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=self.file, stderr=subprocess.DEVNULL, start_new_session=True)
-            # nvidia-smi takes a moment to start on a multi-GPU box: begin the
-            # timed region only once it samples (bounded wait), so that short
-            # regions still get samples; earlier lines are dropped.
-            deadline = time.time() + 10.0
-            while time.time() < deadline and self.proc.poll() is None:
+            # Only this GPU: querying all eight at 100 ms stretched the sampling
+            # period past a short timed region on 8-GPU boxes.
+            targets = [[]]
+            if self.uuid:
+                targets.insert(0, ["-i", self.uuid if self.uuid.startswith("GPU-") else f"GPU-{self.uuid}"])
+            for target in targets:  # this GPU by UUID; all GPUs if nvidia-smi rejects the id
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", *target, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100"],
+                    stdout=self.file, stderr=subprocess.DEVNULL, start_new_session=True)
+                # nvidia-smi takes a moment to start on a multi-GPU box: begin
+                # the timed region only once it samples (bounded wait), so that
+                # short regions still get samples; earlier lines are dropped.
+                deadline = time.time() + 10.0
+                while time.time() < deadline and self.proc.poll() is None:
+                    if Path(self.file.name).stat().st_size > 0:
+                        break
+                    time.sleep(0.02)
                 if Path(self.file.name).stat().st_size > 0:
                     break
-                time.sleep(0.02)
+                if self.proc.poll() is None:  # no sample in time: stop it before the next attempt
+                    os.killpg(self.proc.pid, signal.SIGTERM)
+                    self.proc.wait(timeout=10)
             self.skip = len(Path(self.file.name).read_text().splitlines())
         except Exception:
             self.proc = None
@@ -111,6 +126,8 @@ class Clocks:
             self.proc.wait(timeout=10)
 
     def summary(self):
+        if not self.enabled:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["sampled on rank 0 only"]}
         if self.proc is None or self.file is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
@@ -709,7 +726,7 @@ def run_ours(args, world, rank, local):
         pass
     barrier(world)
     torch.cuda.synchronize(device)
-    with Clocks(uuid) as clocks, torch.cuda.stream(stream):
+    with Clocks(uuid, enabled=rank == 0) as clocks, torch.cuda.stream(stream):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
@@ -959,7 +976,7 @@ def run_tp(args, world, rank, local):
         pass
     barrier(world)
     torch.cuda.synchronize(device)
-    with Clocks(uuid) as clocks, torch.cuda.stream(stream):
+    with Clocks(uuid, enabled=rank == 0) as clocks, torch.cuda.stream(stream):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
