@@ -486,7 +486,7 @@ def reference_ffn_phase_ms(device, geo, weights, replays, lanes=1, ours_latency=
 
 
 def norm_timings(device, geo, replays):
-    """The modulated norm (SURVEY row a1) at S = 392 with per-token time rows,
+    """The modulated norm at S = 392 with per-token time rows,
     CROSS_RESIDUAL and FFN_RESIDUAL modes: this library's op against the
     reference's Triton kernel (baseline/_ref, imported through the stub parent
     package), 30 distinct inputs per replay so that each call reads its rows

@@ -1,5 +1,5 @@
-"""Attention-side projections on the same tcgen05 GEMM engine (SURVEY next
-row f1): the packed QKV projection of ``pre_attn_at_layer_for_compile``
+"""Attention-side projections on the same tcgen05 GEMM engine: the packed QKV
+projection of ``pre_attn_at_layer_for_compile``
 (``WAMInfer/blocks.py:204-208``), the self-attention output projection
 (``blocks.py:218``) and the cross-attention query / output projections
 (``blocks.py:234, 240``).
