@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (BASELINE metric "FFN-stack ms/request and TFLOP/s (2F, 32/120 reuse)"):
+Workload (metric "FFN-stack ms/request and TFLOP/s (2F, 32/120 reuse)"):
 one step = R requests per GPU; one request = the FFN stack of one observation
 under the 2F schedule with 32/120 token reuse -- 30 layers at update 0 (layer 0
 over all 392 rows, layers 1..29 over 32 selected + 240 future + 32 action rows
@@ -756,7 +756,7 @@ def run_ours(args, world, rank, local):
             e1.synchronize()
         latency_ms = max_over_ranks(s1.elapsed_time(e1) / max(1, args.steps // 2), world, device) / args.requests
 
-    # 4F schedule latency (BASELINE config 3 with small coarse motion): the
+    # 4F schedule latency (the motion-adaptive schedule with small coarse motion): the
     # Transformer runs at updates 0, 3, 6 and 9, so a request is the reuse pass
     # of update 0 and three full passes, one request after another on one lane.
     stack.set_down_splits(0)

@@ -1,4 +1,4 @@
-"""The 2F/4F Euler schedule over the FFN stack: the action
+"""The 2F/4F Euler schedule over the FFN stack (the motion-adaptive workload): the action
 latents after 10 updates from the device stack against the CPU oracle's
 schedule, within the FFN tolerance, for a large (2F) and a small (4F) coarse
 motion."""

@@ -46,7 +46,7 @@ def test_stack_equals_chained_blocks(cuda_device):
 
 @pytest.mark.parametrize("count", [32, 64, 96])
 def test_stack_follows_oracle_with_reuse(cuda_device, count):
-    """Capacity buckets of BASELINE config 2 (16 and 32 refreshed rows both use
+    """Capacity buckets of the token-reuse workload (16 and 32 refreshed rows both use
     the 32 bucket; 64; 96): 304, 336 and 368 gathered rows."""
     from waminfer_b200.stack import FFNStack, Geometry, Request, make_weights
 
