@@ -53,10 +53,14 @@ def parse():
     p.add_argument("--down-splits", type=int, default=1,
                    help="split-K of the down projection when lanes > 1 (one lane uses the SM-filling heuristic)")
     p.add_argument("--layers", type=int, default=30)
-    p.add_argument("--cpu-sample-layers", type=int, default=2)
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="minimum host-core time of the CPU baseline sample (whole requests)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-gpu-baselines", action="store_true")
+    p.add_argument("--no-tp", action="store_true",
+                   help="with --gpus N > 1, skip the tensor-parallel line reported beside the headline")
+    p.add_argument("--tp-requests", type=int, default=4, help="requests per step of that tensor-parallel line")
     p.add_argument("--tp", action="store_true",
                    help="tensor-parallel mode: every request's FFN hidden dimension split across the --gpus ranks "
                         "(one all-reduce per layer, strong scaling); not the default bench line")
@@ -184,53 +188,128 @@ def max_over_ranks(value: float, world: int, device) -> float:
 
 
 # ------------------------------------------------------------------ CPU side
-def cpu_baseline(geo, sample_layers: int, min_seconds: float = 10.0):
-    """The reference's native CPU FFN path (Linear -> GELU(tanh) -> Linear in
-    bf16, gather/scatter/gate in torch) restated by the oracle, timed on all
-    host cores over a bounded sample: `sample_layers` reuse layers (M = 304)
-    and `sample_layers` full-refresh layers (M = 392)."""
-    from oracle import cpu_path
-    from waminfer_b200.stack import ffn_flops
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    flops, seconds = cpu_path.time_layers(geo, sample_layers, min_seconds=min_seconds)
-    per_request_s = seconds / flops * geo.request_flops()
+    return platform.processor() or "unknown"
+
+
+class CpuReference:
+    """The reference's own FFN path on the host cores, whole requests: the
+    unmodified WAMInfer package from baseline/_ref (``VideoAdapter.
+    ffn_at_layer_for_compile`` with ``vb.ffn = None``, i.e. its gather,
+    native bf16 ``Linear -> GELU(tanh) -> Linear``, history index_copy / cat
+    and last-layer gate, WAMInfer/blocks.py:246-272, and the history stack of
+    runtime.py:263), driven layer by layer as in baseline/reference_phase.py.
+    The reference's modulated norm is a Triton kernel with no CPU path, so the
+    oracle's torch restatement of it (oracle/ffn.py, rounding points of
+    WAMInfer/_triton_inference.py:149-176) stands in for it on the CPU.
+    A request is the benchmark's: the update-0 pass with 32/120 token reuse
+    and the update-3 full pass, 30 layers each, seeded synthetic bf16 weights."""
+
+    def __init__(self, geo, seed: int = 0):
+        sys.path.insert(0, str(ROOT / "baseline"))
+        import reference_phase as rp
+        from oracle import ffn as offn
+
+        reason = rp.missing(cuda=False)
+        if reason is not None:
+            raise FileNotFoundError(reason)
+        self.geo = geo
+        ref = rp.import_reference(cuda=False)
+        blocks = rp.random_blocks(geo.layers, geo.d, geo.h, "cpu", seed=seed)
+
+        def norm(x, update, mod, previous, time_mod, weight, bias, mode, eps):
+            y, n = offn.modulated_norm(x[0], None if update is None else update[0], mod[0],
+                                       None if previous is None else previous[0], time_mod[0], weight, bias, mode, eps)
+            return y.to(torch.bfloat16)[None], n.to(torch.bfloat16)[None]
+
+        self.phase = rp.ReferencePhase(ref, blocks, "cpu", prepared_rows=None, norm=norm)
+        g = torch.Generator().manual_seed(10_000 + seed)
+        s, d = geo.seq, geo.d
+        self.x = [torch.randn(s, d, generator=g).to(torch.bfloat16) for _ in range(2)]
+        self.time = [(torch.randn(s, 6, d, generator=g) * 0.1).to(torch.bfloat16) for _ in range(2)]
+        chosen = torch.randperm(geo.current, generator=g)[: geo.count].sort().values
+        self.indices = torch.cat((chosen, torch.arange(geo.current, s)))
+        self.history = torch.randn(geo.layers - 1, geo.current, d, generator=g).to(torch.bfloat16)
+
+    def request(self) -> None:
+        geo = self.geo
+        self.phase.run_pass(self.x[0], self.time[0], self.indices, self.history, geo.current, geo.count)
+        self.phase.run_pass(self.x[1], self.time[1])
+
+    def time_requests(self, min_seconds: float, min_requests: int = 1) -> tuple[int, float]:
+        done, t0 = 0, time.perf_counter()
+        while done < min_requests or time.perf_counter() - t0 < min_seconds:
+            self.request()
+            done += 1
+        return done, time.perf_counter() - t0
+
+
+def _cpu_sample(geo, requests: int, seconds: float, threads: int) -> dict:
+    per_request = seconds / requests
     return {
-        "value": flops / seconds / 1e12,
+        "value": geo.request_flops() / per_request / 1e12,
         "unit": "TFLOP/s",
         "cores": threads,
-        "kind": "port",
-        "ms_per_request": per_request_s * 1e3,
-        "sample": f"{sample_layers} reuse layers (M={geo.reuse_rows}) + {sample_layers} full layers (M={geo.seq}) "
-                  f"of one request, bf16 torch CPU GEMMs, scaled to a request by FLOPs "
-                  f"({ffn_flops(geo.reuse_rows, geo.d, geo.h) * sample_layers / 1e12:.2f}+"
-                  f"{ffn_flops(geo.seq, geo.d, geo.h) * sample_layers / 1e12:.2f} TFLOP timed)",
+        "cpu_model": cpu_model(),
+        "kind": "reference",
+        "ms_per_request": per_request * 1e3,
+        "sample": f"{requests} whole request(s) ({2 * geo.layers} FFN layer passes each: update 0 with "
+                  f"{geo.count}/{geo.current} reuse, update 3 full) in {seconds:.1f} s through the reference's own "
+                  f"CPU code path (baseline/_ref VideoAdapter.ffn_at_layer_for_compile, native bf16 FFN; the "
+                  f"Triton norm restated in torch), torch bf16 on {threads} host threads",
     }
 
 
+def cpu_baseline(geo, min_seconds: float = 10.0):
+    """The reference's CPU FFN path timed on all host cores over whole requests
+    (at least `min_seconds` of work after one untimed warm-up request)."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ref = CpuReference(geo)
+    ref.request()
+    requests, seconds = ref.time_requests(min_seconds)
+    return _cpu_sample(geo, requests, seconds, threads)
+
+
 def run_reference(args, world, rank):
+    """The reference arm: the reference's own CPU implementation of the path
+    (CpuReference) on all host threads; each step is one whole request."""
     from waminfer_b200.stack import Geometry
 
     if rank != 0:
         return
     geo = Geometry(layers=args.layers)
-    # Each step is a bounded sample (about 3 s of CPU work) so that the whole
-    # --steps K --warmup W run stays within a few minutes.
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_baseline(geo, 1, min_seconds=0.5)
-    values = []
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    try:
+        ref = CpuReference(geo)
+    except FileNotFoundError as exc:
+        print(json.dumps({"impl": "reference", "unavailable": f"reference CPU path: {exc}"}), flush=True)
+        return
+    for _ in range(max(0, args.warmup)):
+        ref.request()
+    times = []
     for _ in range(args.steps):
-        values.append(cpu_baseline(geo, 1, min_seconds=3.0))
-    value = statistics.median(v["value"] for v in values)
-    base = values[0]
-    ms = geo.request_flops() / (value * 1e12) * 1e3
+        _, seconds = ref.time_requests(0.0, 1)
+        times.append(seconds)
+    total = sum(times)
+    sample = _cpu_sample(geo, len(times), total, threads)
+    value = sample["value"]
+    ms = total / len(times) * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "ms_per_request": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": config_dict(geo, args, world),
-        "cpu_baseline": {**base, "value": value},
+        "cpu_baseline": sample,
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -369,73 +448,22 @@ def reference_ffn_phase_ms(device, geo, weights, replays, lanes=1, ours_latency=
     cap, and a short burst would run faster than a long one); `ours_lanes`
     does the same for the lane throughput (the reference then runs as many
     requests per lane as this library's lanes graph)."""
-    import types
-    from types import SimpleNamespace
-
-    ref_root = ROOT / "baseline" / "_ref"
-    if not (ref_root / "WAMInfer" / "blocks.py").exists():
-        raise FileNotFoundError("baseline/_ref/WAMInfer is not installed")
-    if "WAMInfer" not in sys.modules:
-        pkg = types.ModuleType("WAMInfer")
-        pkg.__path__ = [str(ref_root / "WAMInfer")]
-        sys.modules["WAMInfer"] = pkg
-    if str(ref_root) not in sys.path:
-        sys.path.insert(0, str(ref_root))
-    import wam_infer_ffn_v1 as ext
-    from WAMInfer import blocks as rblocks
-    from WAMInfer import ffn as rffn
-    from WAMInfer._triton_inference import CROSS_RESIDUAL, FFN_RESIDUAL, SELF_INPUT, modulated_norm
-
-    rffn._extension = lambda: ext  # the same extension, prebuilt from the reference's source
-    d, h = geo.d, geo.h
-    blocks = []
-    for w in weights:
-        kw = dict(device=device, dtype=torch.bfloat16)
-        ffn = torch.nn.Sequential(torch.nn.Linear(d, h, **kw), torch.nn.GELU(approximate="tanh"),
-                                  torch.nn.Linear(h, d, **kw)).eval()
-        with torch.no_grad():
-            ffn[0].weight.copy_(w.w_up)
-            ffn[0].bias.copy_(w.b_up)
-            ffn[2].weight.copy_(w.w_down)
-            ffn[2].bias.copy_(w.b_down)
-        blocks.append(SimpleNamespace(ffn=ffn, modulation=w.mod, norm2=SimpleNamespace(eps=1e-6)))
-    native = SimpleNamespace(dit=SimpleNamespace(blocks=blocks), num_layers=len(blocks), training=False)
+    sys.path.insert(0, str(ROOT / "baseline"))
+    import reference_phase as rp
     from waminfer_b200.stack import Request
 
-    zero = torch.zeros(1, geo.seq, d, device=device, dtype=torch.bfloat16)
+    ref = rp.import_reference(cuda=True)
+    blocks = rp.make_blocks(weights, device)
 
     def make_lane(seed):
-        vb = rblocks.VideoAdapter(native)
-        with torch.no_grad():
-            vb.ffn = rffn.PreparedFFN(vb)
-            vb.ffn.prepare(rows=tuple(sorted(set(geo.request_rows()))))
+        phase = rp.ReferencePhase(ref, blocks, device, prepared_rows=geo.request_rows())
         req = Request(geo, device, seed=seed)
-        history = req.history_in[:, None]
-
-        def one_pass(x, time, reuse):
-            extras = {}
-            if reuse:
-                extras = dict(token_reuse=dict(n=geo.current, count=geo.count, cache=history),
-                              token_indices=req.indices, token_outputs=[])
-            state = SimpleNamespace(time_mod=time[None], extras=extras, hidden_states=x[None])
-            for layer, block in enumerate(blocks):
-                pending = state.extras.pop("_inference_ffn_residual", None)
-                update, previous = (None, None) if pending is None else pending
-                xs, _ = modulated_norm(state.hidden_states, update, block.modulation, previous, state.time_mod,
-                                       None, None, SELF_INPUT if pending is None else FFN_RESIDUAL, 1e-6)
-                xs, normalized = modulated_norm(xs, zero, block.modulation, None, state.time_mod, None, None,
-                                                CROSS_RESIDUAL, 1e-6)
-                vb.ffn_at_layer_for_compile(layer, state, normalized, xs)
-            if reuse:
-                torch.stack(state.extras["token_outputs"][1:])
-            return state.hidden_states
 
         def request():
-            with torch.no_grad():
-                one_pass(req.x[0], req.time[0], True)
-                one_pass(req.x[1], req.time[1], False)
+            phase.run_pass(req.x[0], req.time[0], req.indices, req.history_in, geo.current, geo.count)
+            phase.run_pass(req.x[1], req.time[1])
 
-        return vb, request
+        return phase, request
 
     lanes_ = [make_lane(4242 + i) for i in range(lanes)]
     back_to_back = ours_latency[2] if ours_latency is not None else 1
@@ -480,8 +508,8 @@ def reference_ffn_phase_ms(device, geo, weights, replays, lanes=1, ours_latency=
         out["lanes_ms_per_request"] = statistics.median(ref_ms)
         if ours_ms:
             out["ours_lanes_ms"] = statistics.median(ours_ms)
-    for vb, _ in lanes_:
-        vb.ffn.close()
+    for phase, _ in lanes_:
+        phase.close()
     return out
 
 
@@ -859,7 +887,7 @@ def run_ours(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(geo, args.cpu_sample_layers)
+        cpu = cpu_baseline(geo, args.cpu_seconds)
     baselines = None
     if rank == 0 and world == 1 and not args.no_gpu_baselines:
         # A one-lane graph of 8 back-to-back requests, timed in alternation
@@ -904,16 +932,26 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches, "launches_per_request": stack.launches_per_request(),
             "library_launches_total": _lib.launch_count(),
         }
-        print(json.dumps(line), flush=True)
     graph.reset()
     latency_graph.reset()
     stack.close()
+    del stack, graph, latency_graph, requests, weights
+    tp = None
+    if world > 1 and not args.no_tp:
+        # The secondary tensor-parallel mode on the same ranks, reported beside
+        # the request-parallel headline with its own timing and clock record.
+        torch.cuda.empty_cache()
+        tp = run_tp(args, world, rank, local, requests=args.tp_requests, report=False)
+    if rank == 0:
+        line["tp"] = tp
+        print(json.dumps(line), flush=True)
 
 
-def run_tp(args, world, rank, local):
+def run_tp(args, world, rank, local, requests: int | None = None, report: bool = True):
     """Tensor-parallel arm: the same requests on every rank, h split across
     the ranks, one all-reduce per layer.  Whole-job TFLOP/s counts each
-    request's FLOPs once (strong scaling)."""
+    request's FLOPs once (strong scaling).  Returns rank 0's line (printed
+    when `report`)."""
     import torch.distributed as dist
 
     from waminfer_b200.stack import Geometry, Request, make_weights
@@ -931,7 +969,8 @@ def run_tp(args, world, rank, local):
         from waminfer_b200.stack import FFNStack
 
         stack = FFNStack(shards, geo, device)
-    requests = [Request(geo, device, seed=i) for i in range(args.requests)]
+    n_requests = args.requests if requests is None else requests
+    requests = [Request(geo, device, seed=i) for i in range(n_requests)]
     stream = torch.cuda.Stream(device)
 
     def step():
@@ -986,25 +1025,28 @@ def run_tp(args, world, rank, local):
     torch.cuda.synchronize(device)
     barrier(world)
     ms_step = max_over_ranks(start.elapsed_time(end) / args.steps, world, device)
-    flops_step = geo.request_flops() * args.requests
+    flops_step = geo.request_flops() * n_requests
+    line = None
     if rank == 0:
         line = {
             "metric": METRIC, "impl": "ours-tp", "value": flops_step / (ms_step * 1e-3) / 1e12, "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "ms_per_request": ms_step / args.requests, "higher_is_better": True, "scaling": "strong",
+            "ms_per_request": ms_step / n_requests, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights)",
             "config": dict(config_dict(geo, args, 1), parallelism=f"tp{world} (h split, one all-reduce per layer)",
-                           requests_per_step=args.requests, capture=mode),
+                           requests_per_step=n_requests, requests_per_gpu_per_step=n_requests, capture=mode),
             "clocks": clocks.summary(),
-            "gpu_launches": stack.launches_per_request() * args.requests * args.steps,
+            "gpu_launches": stack.launches_per_request() * n_requests * args.steps,
         }
-        print(json.dumps(line), flush=True)
+        if report:
+            print(json.dumps(line), flush=True)
     if graph is not None:
         graph.reset()
     del graph
     stack.close()
     if world > 1:
         dist.barrier()
+    return line
 
 
 def main():

@@ -154,7 +154,13 @@ int wamffn_linear_status(wamffn_linear_plan* plan, uint32_t* status, int clear);
  * clears on `stream` when `status` is null.  `status` may instead point at a
  * caller-owned device word (4-byte aligned, cleared by the caller) that the
  * kernels OR WAMFFN_DEV_* bits into; with null the bits land in the shared
- * word and are not reported.
+ * word and are not reported, so a null `status` gives up error detection: a
+ * call whose GEMM gave up on a timed-out pipeline wait writes no partials,
+ * and its reduction then returns the previous call's result without any error.
+ *
+ * The array's address is looked up once per device and kept: calls after
+ * cudaDeviceReset (or any teardown of the device's primary context) are not
+ * supported.
  * ---------------------------------------------------------------------- */
 #define WAMFFN_STATIC_SCRATCH_BYTES (16u << 20) /* 16 MiB per device */
 int wamffn_linear_run_static(int device, void* stream, int rows, int n_out, int k_in, int splits,

@@ -26,26 +26,30 @@ def fresh_updates(nfe: int) -> list[int]:
     return [0, 3] if nfe == 2 else [0, 3, 6, 9]
 
 
-def stack_pass(x, time, weights, indices=None, history=None, cache_rows=0, eps=1e-6):
+def stack_pass(x, time, weights, indices=None, history=None, cache_rows=0, eps=1e-6, device="cpu"):
     """All layers of one pass on the fp32 oracle; layer 0 recomputes every
-    row, later layers gather `indices` and read history[layer - 1]."""
-    x = x.float()
+    row, later layers gather `indices` and read history[layer - 1].  The fp32
+    arithmetic runs on `device` (a GPU holding the weights keeps a 30-layer
+    oracle fast; matmuls there must run without TF32)."""
+    x = x.float().to(device)
+    time = time.float().to(device)
     for layer, w in enumerate(weights):
         reuse = indices is not None and layer > 0
-        cache = history[layer - 1].float() if reuse else None
+        cache = history[layer - 1].float().to(device) if reuse else None
         x, _, _, _ = offn.ffn_block(
-            x, None, None, w.mod[0].float().cpu(), time, w.w_up, w.b_up, w.w_down, w.b_down,
+            x, None, None, w.mod[0].float().to(device), time, w.w_up, w.b_up, w.w_down, w.b_down,
             indices if reuse else None, cache, cache_rows if reuse else 0, eps,
-            ffn=lambda a, wu, bu, wd, bd: offn.prepared_ffn(a, wu.cpu(), bu.cpu(), wd.cpu(), bd.cpu()))
+            ffn=lambda a, wu, bu, wd, bd: offn.prepared_ffn(a, wu.to(device), bu.to(device), wd.to(device),
+                                                            bd.to(device)))
     return offn.bf16(x)
 
 
 def run_euler(weights, video, actions, times, indices, history, cache_rows, amplitude_m, threshold_m=0.05,
-              eps=1e-6):
+              eps=1e-6, device="cpu"):
     """times: {update: [seq, 6, d]} for the fresh updates.  Returns
-    (actions after update 10, fresh updates, nfe)."""
-    a = offn.bf16(actions.float())
-    video = video.float()
+    (actions after update 10, fresh updates, nfe) on `device`."""
+    a = offn.bf16(actions.float().to(device))
+    video = video.float().to(device)
     nfe = 2
     residual = None
     fresh = []
@@ -55,7 +59,7 @@ def run_euler(weights, video, actions, times, indices, history, cache_rows, ampl
         if k in fresh_updates(nfe):
             fresh.append(k)
             y = stack_pass(x, times[k].float(), weights, indices if k == 0 else None,
-                           history if k == 0 else None, cache_rows if k == 0 else 0, eps)
+                           history if k == 0 else None, cache_rows if k == 0 else 0, eps, device)
             residual = offn.bf16(y - x)
         else:
             y = offn.bf16(x + residual)

@@ -96,21 +96,25 @@ def ffn_block(x, update, normalized, mod, time, w_up, b_up, w_down, b_down, indi
     else:
         y, n = x.float(), normalized.float()
     S, d = y.shape
+    dev = y.device
     if indices is None:
-        idx = torch.arange(S)
+        idx = torch.arange(S, device=dev)
     else:
-        idx = torch.as_tensor(indices).long()
+        idx = torch.as_tensor(indices).long().to(dev)
     pad = idx < 0
     a = n[idx.clamp_min(0)]
     a[pad] = 0.0
-    o = ffn(a, w_up, b_up, w_down, b_down)
-    output = torch.zeros(S, d)
+    o = ffn(a, w_up, b_up, w_down, b_down).to(dev)
+    output = torch.zeros(S, d, device=dev)
     if cache_rows > 0 and cache is not None:
-        output[:cache_rows] = cache.float()
-    for j in range(idx.numel()):  # later entries win on duplicates
-        r = int(idx[j])
-        if r >= 0:
-            output[r] = o[j]
+        output[:cache_rows] = cache.float().to(dev)
+    # index_copy semantics with later entries winning on duplicates: each row
+    # takes the last gather slot j that names it.
+    slots = torch.arange(idx.numel(), device=dev)
+    last = torch.full((S,), -1, dtype=torch.long, device=dev)
+    last.scatter_reduce_(0, idx[~pad], slots[~pad], reduce="amax")
+    rows = torch.nonzero(last >= 0).flatten()
+    output[rows] = o[last[rows]]
     clean = output[:cache_rows].clone() if cache_rows > 0 else None
     x_next = gate_residual(y, output, mod, time)
     return x_next, output, clean, o

@@ -125,3 +125,61 @@ def test_rgb_mandatory_device_threshold_and_random(cuda_device):
     with pytest.raises(ValueError, match="split"):
         TokenReuse.mandatory_rows_device(torch.zeros(385, 320, 3, dtype=torch.uint8, device=cuda_device),
                                          torch.zeros(385, 320, 3, dtype=torch.uint8, device=cuda_device), 12, 10)
+
+
+def test_select_tokens_near_ties(cuda_device, golden):
+    """Constructed near-ties (equal float32 scores with different exact
+    ratios, rows 1-2 ulps apart, zero rows, mandatory rows; cut inside each
+    group): the device indices equal the reference's (fixture made by its own
+    select_tokens) and the oracle's."""
+    from waminfer_b200.approximation import select_tokens
+
+    g = golden("near_ties.pt")
+    n = 120
+    for case in g["cases"]:
+        features = torch.zeros(1, case["seq"], g["now"].shape[-1], dtype=torch.bfloat16, device=cuda_device)
+        features[0, :n] = g["now"].to(cuda_device)
+        reuse = dict(n=n, count=case["count"], mandatory=case["mandatory"].to(cuda_device),
+                     features=g["before"][None].to(cuda_device))
+        state = SimpleNamespace(extras=dict(token_reuse=reuse))
+        select_tokens(state, features)
+        got = state.extras["token_indices"].cpu().tolist()
+        assert got == case["indices"].tolist(), case["name"]
+        ref = oreuse.token_indices(g["now"].float().numpy(), g["before"].float().numpy(), case["mandatory"].numpy(),
+                                   case["count"], n, case["seq"])
+        assert got == ref.tolist(), case["name"]
+
+
+def test_select_tokens_vs_installed_reference_on_gpu(cuda_device, golden):
+    """The reference's own select_tokens (the unmodified package in
+    baseline/_ref) run on this GPU against the device kernel: the near-tie
+    fixture and seeded random features at the capacity buckets."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "baseline"))
+    import reference_phase as rp
+
+    if rp.missing(cuda=False):
+        pytest.skip(rp.missing(cuda=False))
+    ref = rp.import_reference(cuda=False)
+    from waminfer_b200.approximation import select_tokens
+
+    g = golden("near_ties.pt")
+    cases = [(g["now"], g["before"], c["mandatory"], c["count"], c["seq"]) for c in g["cases"]]
+    gen = torch.Generator().manual_seed(77)
+    for count in (32, 64, 96, 1, 119):
+        before = torch.randn(120, 3072, generator=gen).to(torch.bfloat16)
+        now = (before.float() + torch.randn(120, 3072, generator=gen) * torch.rand(120, 1, generator=gen)).to(
+            torch.bfloat16)
+        cases.append((now, before, torch.rand(120, generator=gen) < 0.05, count, 392))
+    for now, before, mandatory, count, seq in cases:
+        results = []
+        for fn in (ref.approximation.select_tokens, select_tokens):
+            features = torch.zeros(1, seq, now.shape[-1], dtype=torch.bfloat16, device=cuda_device)
+            features[0, :120] = now.to(cuda_device)
+            reuse = dict(n=120, count=count, mandatory=mandatory.to(cuda_device), features=before[None].to(cuda_device))
+            state = SimpleNamespace(extras=dict(token_reuse=reuse))
+            fn(state, features)
+            results.append(state.extras["token_indices"].cpu().tolist())
+        assert results[0] == results[1], count

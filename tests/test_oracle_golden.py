@@ -122,3 +122,38 @@ def test_motion_schedule(golden):
     for motion, steps in full.items():
         expected = [0, 3] if motion > 0.08 else [0, 3, 6, 9]
         assert steps == expected, motion
+
+
+def test_select_tokens_near_ties(golden):
+    """Constructed near-ties (tests/golden/make_near_ties.py): a group of rows
+    with one float32 score but different exact ratios, rows 1 and 2 ulps above
+    and 1 ulp below it, zero rows, mandatory rows; the cut placed inside each
+    group.  The restated fixed-order sums give the reference's indices."""
+    g = golden("near_ties.pt")
+    now, before = g["now"].float().numpy(), g["before"].float().numpy()
+    got_scores = oreuse.scores(now, before)
+    assert got_scores.tolist() == g["scores"].tolist()
+    labels = g["labels"]
+    tie = [i for i, lab in enumerate(labels) if lab == "tie"]
+    assert len({float(got_scores[i]) for i in tie}) == 1 and len(tie) == 10
+    for lab, steps in (("plus1", 1), ("plus2", 2), ("minus1", -1)):
+        rows = [i for i, x in enumerate(labels) if x == lab]
+        assert all(got_scores[i] == np.float32(g["s0"] + steps * g["ulp"]) for i in rows), lab
+    for case in g["cases"]:
+        idx = oreuse.token_indices(now, before, case["mandatory"].numpy(), case["count"], 120, case["seq"])
+        assert idx.tolist() == case["indices"].tolist(), case["name"]
+
+
+def test_fixed_order_sum_is_exact_for_bf16_rows():
+    """The fixed-order float64 accumulation equals the exact (math.fsum) sum
+    rounded to float32 for bf16 rows of the benchmark's dimension."""
+    import math
+
+    rng = np.random.default_rng(5)
+    for scale in (1e-3, 1.0, 100.0):
+        a = torch.from_numpy(rng.standard_normal((8, 3072)) * scale).to(torch.bfloat16).float().numpy()
+        b = torch.from_numpy(rng.standard_normal((8, 3072)) * scale).to(torch.bfloat16).float().numpy()
+        terms = np.abs(a - b)
+        got = oreuse._row_sums_fixed_order(terms)
+        exact = np.array([math.fsum(map(float, row)) for row in terms]).astype(np.float32)
+        assert got.tolist() == exact.tolist(), scale

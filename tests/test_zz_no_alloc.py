@@ -38,11 +38,20 @@ def test_static_rejects_what_does_not_fit_before_launching():
     # Split counts outside [2, 16].
     assert _run_static(lib, 0, None, 128, 3072, 14336, 1, 0, fake, fake, fake, fake) == 1
     assert _run_static(lib, 0, None, 128, 3072, 14336, 17, 0, fake, fake, fake, fake) == 1
+    # One row past the limit: 4 x 342 x 3072 x 4 B + 256 > 16 MiB (341 rows fit, the GPU test runs them).
+    assert HEADER + 4 * 342 * 3072 * 4 > SCRATCH_BYTES >= HEADER + 4 * 341 * 3072 * 4
+    assert _run_static(lib, 0, None, 342, 3072, 14336, 4, 0, fake, fake, fake, fake) == 1
+    assert b"static scratch" in lib.wamffn_last_error()
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("rows,packed", [(128, True), (392, False)])
-def test_static_matches_plan_on_two_calls_in_a_row(cuda_device, rows, packed):
+@pytest.mark.parametrize("rows,packed,splits", [(1, True, None), (77, False, None), (128, True, None),
+                                                (392, True, None), (392, False, None), (341, True, 4)])
+def test_static_matches_plan_on_two_calls_in_a_row(cuda_device, rows, packed, splits):
+    """Against the plan path and the fp32 oracle (x . W^T + b in fp32, rounded
+    to bf16), two calls in a row with different inputs.  Row counts that are
+    not a multiple of 16 leave padded token columns; 341 rows at 4 splits
+    fill the scratch to within 17 KB of its size."""
     from waminfer_b200.ffn import pack_weight
 
     lib = _lib.lib()
@@ -59,9 +68,10 @@ def test_static_matches_plan_on_two_calls_in_a_row(cuda_device, rows, packed):
         values = (ctypes.c_uint32 * 7)()
         _lib.check(lib.wamffn_linear_configuration(plan, values, 7))
         # The plan's own split count when it fits the static scratch, else the largest that does.
-        splits = int(values[4])
-        while splits > 2 and HEADER + splits * rows * n_out * 4 > SCRATCH_BYTES:
-            splits -= 1
+        if splits is None:
+            splits = max(2, int(values[4]))
+            while splits > 2 and HEADER + splits * rows * n_out * 4 > SCRATCH_BYTES:
+                splits -= 1
         assert splits >= 2 and HEADER + splits * rows * n_out * 4 <= SCRATCH_BYTES
         stream = torch.cuda.current_stream(cuda_device).cuda_stream
         status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
@@ -79,6 +89,9 @@ def test_static_matches_plan_on_two_calls_in_a_row(cuda_device, rows, packed):
             torch.cuda.synchronize(cuda_device)
             ok, msg = offn.check_close(out, ref)
             assert ok, f"call {call}, splits {splits}: {msg}"
+            oracle = offn.bf16(x.float() @ weight.float().T + bias.float())
+            ok, msg = offn.check_close(out, oracle)
+            assert ok, f"call {call}, splits {splits}, against the oracle: {msg}"
         assert int(status.item()) == 0
     finally:
         lib.wamffn_linear_plan_destroy(plan)

@@ -5,6 +5,19 @@
 // score (ties: smaller index first, i.e. a stable descending sort) are written
 // in ascending order, followed by the future rows n..seq-1.
 //
+// Summation order (restated element for element by oracle/reuse.py::scores,
+// so indices equal the oracle's in every case, near-ties included): each term
+// is formed in fp32 as the reference forms it (|now - before| and
+// |now| + |before| of bf16 values widened to fp32) and accumulated in fp64.
+// Lane l of the row's warp adds the 8-element chunks l, l + 32, l + 64, ...
+// in order, element by element; the 32 lane sums are combined by the xor
+// butterfly (offsets 16, 8, 4, 2, 1); each total is rounded once to fp32.
+// For bf16 activations of magnitude >= 2^-30 (or 0) every term's lowest bit
+// is at or above 2^-37 and the fp64 running sum of a 3072-element row stays
+// exact, so the fp32 totals are the correctly rounded exact sums: equal to the
+// reference's fp32 sums whenever those are exact (whatever torch's reduction
+// order), and independent of this kernel's order.
+//
 // One CTA: n <= 1024 rows of the current frame.  Ranking is an all-pairs count
 // (n^2 comparisons), which is exact and order-independent.
 #pragma once
@@ -40,7 +53,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_tokens_kernel(const Sel
   for (int r = warp; r < p.n; r += nwarps) {
     const __nv_bfloat16* a = p.now + size_t(r) * p.now_stride;
     const __nv_bfloat16* b = p.before + size_t(r) * p.dim;
-    float num = 0.f, den = 0.f;
+    double num = 0.0, den = 0.0;
     for (int e = lane * 8; e < p.dim; e += 32 * 8) {
       const uint4 ua = *reinterpret_cast<const uint4*>(a + e);
       const uint4 ub = *reinterpret_cast<const uint4*>(b + e);
@@ -51,17 +64,21 @@ __global__ void __launch_bounds__(kSelectThreads) select_tokens_kernel(const Sel
       for (int i = 0; i < 4; ++i) {
         const float2 fa = __bfloat1622float2(ha[i]);
         const float2 fb = __bfloat1622float2(hb[i]);
-        num += fabsf(fa.x - fb.x) + fabsf(fa.y - fb.y);
-        den += (fabsf(fa.x) + fabsf(fb.x)) + (fabsf(fa.y) + fabsf(fb.y));
+        // fp32 terms exactly as the reference forms them; no contraction into the fp64 adds.
+        num = __dadd_rn(num, double(fabsf(__fsub_rn(fa.x, fb.x))));
+        num = __dadd_rn(num, double(fabsf(__fsub_rn(fa.y, fb.y))));
+        den = __dadd_rn(den, double(__fadd_rn(fabsf(fa.x), fabsf(fb.x))));
+        den = __dadd_rn(den, double(__fadd_rn(fabsf(fa.y), fabsf(fb.y))));
       }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      num += __shfl_xor_sync(0xffffffffu, num, o);
-      den += __shfl_xor_sync(0xffffffffu, den, o);
+      num = __dadd_rn(num, __shfl_xor_sync(0xffffffffu, num, o));
+      den = __dadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
     }
     if (lane == 0) {
-      float s = (2.0f * num) / fmaxf(den, 1e-6f);
+      const float nf = __double2float_rn(num), df = __double2float_rn(den);
+      float s = __fdiv_rn(__fmul_rn(2.0f, nf), fmaxf(df, 1e-6f));
       if (p.mandatory && p.mandatory[r]) s = __int_as_float(0x7f800000);  // +inf
       score[r] = s;
     }
