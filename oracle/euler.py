@@ -45,9 +45,16 @@ def stack_pass(x, time, weights, indices=None, history=None, cache_rows=0, eps=1
 
 
 def run_euler(weights, video, actions, times, indices, history, cache_rows, amplitude_m, threshold_m=0.05,
-              eps=1e-6, device="cpu"):
+              eps=1e-6, device="cpu", pass_fn=None):
     """times: {update: [seq, 6, d]} for the fresh updates.  Returns
-    (actions after update 10, fresh updates, nfe) on `device`."""
+    (actions after update 10, fresh updates, nfe) on `device`.
+
+    pass_fn(x, time, indices, history, cache_rows) -> y replaces the oracle's
+    FFN stack (default: ``stack_pass`` over `weights`); a test passes another
+    implementation's stack to run the same schedule on it."""
+    if pass_fn is None:
+        def pass_fn(x, time, idx, hist, n):
+            return stack_pass(x, time, weights, idx, hist, n, eps, device)
     a = offn.bf16(actions.float().to(device))
     video = video.float().to(device)
     nfe = 2
@@ -58,8 +65,8 @@ def run_euler(weights, video, actions, times, indices, history, cache_rows, ampl
         x = torch.cat((video, a))
         if k in fresh_updates(nfe):
             fresh.append(k)
-            y = stack_pass(x, times[k].float(), weights, indices if k == 0 else None,
-                           history if k == 0 else None, cache_rows if k == 0 else 0, eps, device)
+            y = pass_fn(x, times[k].float(), indices if k == 0 else None, history if k == 0 else None,
+                        cache_rows if k == 0 else 0).float().to(device)
             residual = offn.bf16(y - x)
         else:
             y = offn.bf16(x + residual)
