@@ -116,7 +116,11 @@ int wamffn_linear_run(wamffn_linear_plan* plan, void* stream, const void* x, con
                       const void* bias, void* out);
 
 /* Replaces Plan::selected_configuration (cpp:189).  Writes up to n values:
- * {feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned}. */
+ * {feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned,
+ *  streamk_groups}.  streamk_groups > 0: a GELU plan whose feature tiles
+ * leave SMs idle runs as stream-K, its tiles' K blocks cut into that many
+ * equal ranges, one per CTA pair on every SM, with a fixed-order fix-up of
+ * the split tiles (deterministic). */
 int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values, int n);
 
 /* Reads (and with clear != 0 resets) the device status word of a plan.
@@ -274,8 +278,20 @@ int wamffn_block_status(wamffn_block_plan* plan, uint32_t* status, int clear);
  * partials through L2.  Applies to launches enqueued after the call. */
 int wamffn_block_plan_set_splits(wamffn_block_plan* plan, int rows, int splits);
 /* {up: feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned,
- *  down: same 7 values} for a given row count. */
+ *  down: same 7 values, up streamk_groups, down streamk_groups} for a given
+ * row count (n = 14 omits the last two). */
 int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t* values, int n);
+/* Stream-K up projection on or off (default off; WAMFFN_STREAMK=1 changes
+ * the default of new plans) for launches enqueued after the call.  No
+ * counterpart in the reference (cuBLASLt picks its own schedule inside
+ * Plan::tune).  With it the up projection's 56 feature-tile pairs
+ * (h = 14336) are spread over every SM pair instead of leaving 36 SMs idle;
+ * on B200 that measured slower (48 vs 36 us at 392 rows: the operand streams
+ * of 148 SMs arrive more slowly per K block, and the split tiles' fp32
+ * partials cross L2 twice).  Results differ from the data-parallel grid in
+ * the last bits (a different fp32 summation order), so a caller that compares
+ * lanes bit for bit sets the same schedule on every plan. */
+int wamffn_block_plan_set_streamk(wamffn_block_plan* plan, int enabled);
 
 /* ------------------------------------------------------------------------
  * FFN stack: the FFN phases of `layers` consecutive DiT layers in one call,

@@ -272,3 +272,45 @@ def norm_close(n, ref, what):
     diff = (n.float() - ref.float()).abs()
     assert float(diff.max()) <= 2.0**-5, (what, float(diff.max()))
     assert float((diff > 0).float().mean()) <= 0.01, (what, float((diff > 0).float().mean()))
+
+
+def test_streamk_gelu_plans_follow_oracle(cuda_device, tmp_path):
+    """Stream-K GELU plans (WAMFFN_STREAMK=1, read once per process, so in a
+    child interpreter): single-CTA tiles (odd tile counts) with up to four
+    helper pieces per owner tile, and the FFN up projection on UMMA pairs,
+    against the fp32 oracle; the plans report their stream-K grid."""
+    import os
+    import subprocess
+    import sys
+
+    script = tmp_path / "sk.py"
+    script.write_text(
+        "import torch\n"
+        "from oracle import ffn as offn\n"
+        "from waminfer_b200.ffn import Plan\n"
+        "dev = torch.device('cuda', 0)\n"
+        "torch.backends.cuda.matmul.allow_tf32 = False\n"
+        "g = torch.Generator(device=dev).manual_seed(5)\n"
+        "for rows, n_out, k_in in ((1, 384, 256), (100, 384, 1024), (300, 640, 512), (512, 128, 3072),\n"
+        "                          (392, 14336, 3072), (304, 14336, 3072), (77, 14336, 3072)):\n"
+        "    x = torch.randn(rows, k_in, device=dev, generator=g).bfloat16()\n"
+        "    w = (torch.randn(n_out, k_in, device=dev, generator=g) * 0.02).bfloat16()\n"
+        "    b = (torch.randn(n_out, device=dev, generator=g) * 0.01).bfloat16()\n"
+        "    plan = Plan(x, w, b, exhaustive=False, gelu=True)\n"
+        "    import ctypes\n"
+        "    from waminfer_b200 import _lib\n"
+        "    vals = (ctypes.c_uint32 * 8)()\n"
+        "    _lib.check(_lib.lib().wamffn_linear_configuration(plan._handle, vals, 8))\n"
+        "    assert vals[7] > 0, (rows, n_out, k_in, list(vals))\n"
+        "    for _ in range(2):\n"
+        "        out = plan.run(x, w, b)\n"
+        "        ref = offn.bf16(offn.gelu_tanh(x.float() @ w.float().T + b.float()))\n"
+        "        ok, msg = offn.check_close(out, ref)\n"
+        "        assert ok, (rows, n_out, k_in, msg)\n"
+        "    assert plan.status() == 0\n"
+        "    plan.close()\n"
+        "print('ok')\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, WAMFFN_STREAMK="1", PYTHONPATH=root)
+    out = subprocess.run([sys.executable, str(script)], env=env, cwd=root, timeout=600, capture_output=True, text=True)
+    assert out.returncode == 0, out.stdout + out.stderr

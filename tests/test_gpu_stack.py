@@ -117,7 +117,8 @@ def test_persistent_pass_kernel_equals_three_kernel_stack(cuda_device, tmp_path)
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     results = {}
     for flag in ("0", "1"):
-        env = dict(os.environ, WAMFFN_PASS=flag, PYTHONPATH=root)
+        # The pass kernel runs the data-parallel up projection (the stack's default grid).
+        env = dict(os.environ, WAMFFN_PASS=flag, WAMFFN_STREAMK="0", PYTHONPATH=root)
         out = tmp_path / f"pass{flag}.pt"
         subprocess.run([sys.executable, str(script), str(out)], check=True, env=env, cwd=root, timeout=600)
         results[flag] = torch.load(out)
@@ -128,7 +129,7 @@ def test_persistent_pass_kernel_equals_three_kernel_stack(cuda_device, tmp_path)
 
     # The same stack with one CTA per 128-feature tile (WAMFFN_PAIR=0, no UMMA
     # pairs): the same sums per element, within the stack tolerance.
-    env = dict(os.environ, WAMFFN_PASS="0", WAMFFN_PAIR="0", PYTHONPATH=root)
+    env = dict(os.environ, WAMFFN_PASS="0", WAMFFN_PAIR="0", WAMFFN_STREAMK="0", PYTHONPATH=root)
     out = tmp_path / "nopair.pt"
     subprocess.run([sys.executable, str(script), str(out)], check=True, env=env, cwd=root, timeout=600)
     single = torch.load(out)
@@ -195,3 +196,56 @@ def test_set_splits_validation(cuda_device):
         with pytest.raises(_lib.WamffnError, match="outside"):
             plan.set_splits(rows, splits)
     plan.close()
+
+
+@pytest.mark.parametrize("count", [32, 96])
+def test_streamk_up_projection_matches_data_parallel(cuda_device, count):
+    """The stream-K up projection (56 tile pairs over all 74 SM pairs, helper
+    partials added in K order) against the data-parallel grid and the
+    oracle, on a 3-layer stack with token reuse (layer 0 at 392 rows, then
+    304 / 368); graph replay of the stream-K stack is bit-identical."""
+    from waminfer_b200.stack import FFNStack, Geometry, Request, make_weights
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    geo = Geometry(layers=3, count=count)
+    weights = make_weights(geo.layers, geo.d, geo.h, cuda_device, seed=12)
+    stack = FFNStack(weights, geo, cuda_device)
+    req = Request(geo, cuda_device, seed=13)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    outs = {}
+    for sk in (True, False):
+        stack.set_streamk(sk)
+        cfg = stack.plan.configuration(geo.reuse_rows)["up"]
+        assert (cfg["streamk_groups"] > 0) == sk, cfg
+        stack.enqueue_pass(req.x[0], req.out[0], req.time[0], stream, reuse=req)
+        stack.enqueue_pass(req.x[1], req.out[1], req.time[1], stream)
+        torch.cuda.synchronize()
+        assert stack.plan.status() == 0
+        outs[sk] = (req.out[0].clone(), req.out[1].clone(), req.history_out.clone())
+    for a, b in zip(outs[True], outs[False]):
+        ok, msg = offn.check_close(a, b.float(), max_abs=6e-2)
+        assert ok, msg
+    # Against the oracle, full-refresh pass.
+    x = req.x[1].float()
+    for w in weights:
+        x, _, _, _ = offn.ffn_block(x, None, None, w.mod[0].float(), req.time[1].float(), w.w_up, w.b_up, w.w_down,
+                                    w.b_down, None, None, 0, 1e-6,
+                                    ffn=lambda a, wu, bu, wd, bd: offn.prepared_ffn(a, wu, bu, wd, bd))
+    ok, msg = offn.check_close(outs[True][1], x, max_abs=6e-2)
+    assert ok, msg
+    # Deterministic: a captured stream-K request replays to the same bits.
+    stack.set_streamk(True)
+    side = torch.cuda.Stream(cuda_device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        stack.enqueue_pass(req.x[0], req.out[0], req.time[0], side.cuda_stream, reuse=req)
+        stack.enqueue_pass(req.x[1], req.out[1], req.time[1], side.cuda_stream)
+    for _ in range(2):
+        for t in (*req.out, req.history_out):
+            t.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert all(torch.equal(a, b) for a, b in zip((req.out[0], req.out[1], req.history_out), outs[True]))
+    assert stack.plan.status() == 0
+    graph.reset()
+    stack.close()

@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "wamffn_block_status",
     "wamffn_block_configuration",
     "wamffn_block_plan_set_splits",
+    "wamffn_block_plan_set_streamk",
     "wamffn_rgb_mandatory",
     "wamffn_select_tokens",
     "wamffn_pack_weight",
@@ -201,6 +202,7 @@ def _declare(lib):
     lib.wamffn_block_status.argtypes = [vp, u32p, i]
     lib.wamffn_block_configuration.argtypes = [vp, i, u32p, i]
     lib.wamffn_block_plan_set_splits.argtypes = [vp, i, i]
+    lib.wamffn_block_plan_set_streamk.argtypes = [vp, i]
     lib.wamffn_rgb_mandatory.argtypes = [vp, vp, vp, i, i, i, i, vp]
     lib.wamffn_select_tokens.argtypes = [vp, ctypes.POINTER(SelectArgs)]
     lib.wamffn_pack_weight.argtypes = [vp, vp, vp, i, i]

@@ -69,10 +69,17 @@ class BlockPlan:
         _lib.check(_lib.lib().wamffn_block_run(self.handle, stream, ctypes.byref(args)))
 
     def configuration(self, rows: int) -> dict:
-        values = (ctypes.c_uint32 * 14)()
-        _lib.check(_lib.lib().wamffn_block_configuration(self.handle, rows, values, 14))
+        values = (ctypes.c_uint32 * 16)()
+        _lib.check(_lib.lib().wamffn_block_configuration(self.handle, rows, values, 16))
         names = ("feature_tile", "token_pad", "mma_count", "stages", "split_k", "tmem_columns", "tuned")
-        return {"up": dict(zip(names, values[:7])), "down": dict(zip(names, values[7:]))}
+        up, down = dict(zip(names, values[:7])), dict(zip(names, values[7:14]))
+        up["streamk_groups"], down["streamk_groups"] = values[14], values[15]
+        return {"up": up, "down": down}
+
+    def set_streamk(self, enabled: bool) -> None:
+        """Stream-K up projection (every SM pair takes an equal range of the
+        tiles' K blocks) on or off for launches enqueued from now on."""
+        _lib.check(_lib.lib().wamffn_block_plan_set_streamk(self.handle, 1 if enabled else 0))
 
     def set_splits(self, rows: int, splits: int) -> None:
         """Down-projection split-K factor for `rows` gathered rows (0: all row

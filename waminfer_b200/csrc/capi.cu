@@ -145,9 +145,13 @@ int prepare_device(int device, int* sm_count) {
                   device, major, minor);
     WAMFFN_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, device));
     DeviceGuard g(device);
-    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemLimit));
-    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemLimit));
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemLimit));
+    WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemLimit));
     cudaFuncAttributes pass_attr{};
     WAMFFN_CUDA(cudaFuncGetAttributes(&pass_attr, stack_pass_kernel));  // its static barriers count too
@@ -169,7 +173,38 @@ struct GemmConfig {
   int a_stages = 0, b_stages = 0, splits = 1;
   uint32_t tmem_cols = 0;
   int smem_bytes = 0;
+  int sk = 0;  // stream-K CTA groups (pairs with group == 2); 0 = data-parallel grid
 };
+
+// Stream-K is opt-in: on B200 it measured slower for the FFN up projection
+// (48 vs 36 us at M = 392): with all 148 SMs streaming, each K block's
+// operands arrive more slowly (0.72 vs 0.63 us per block), and the helper
+// dump and the owner's fix-up move 30 MB of fp32 partials through L2.
+bool streamk_enabled() {
+  static const bool on = env_flag("WAMFFN_STREAMK", false);
+  return on;
+}
+
+// Stream-K size for a bias / GELU GEMM whose feature tiles leave SMs idle:
+// one range of K blocks per CTA group on every SM, each range within one
+// tile's K extent, at most kMaxSkHelpers helper pieces per owner tile.
+// 0 when the data-parallel grid already fills the machine.
+int streamk_groups(const GemmConfig& c, int sm_count) {
+  if (c.splits != 1 || c.groups != 1) return 0;
+  const int tiles = c.n_out / (kFeatTile * c.group);
+  const int kb = c.k_in / kBlockK;
+  const long long units = (long long)tiles * kb;
+  for (int g = sm_count / c.group; g > tiles; --g) {
+    const long long per = units / g;  // shortest range
+    if (per < 1) continue;
+    const long long helpers = (kb + per - 1) / per;
+    if (helpers <= kMaxSkHelpers && (units + g - 1) / g <= kb) return g;
+  }
+  return 0;
+}
+
+// Bytes of stream-K workspace (helper slots) a plan holds for tok_pad tokens.
+size_t streamk_ws_bytes(int sm_count, int tok_pad) { return size_t(sm_count) * tok_pad * kFeatTile * sizeof(float); }
 
 bool pair_enabled() {
   static const bool on = env_flag("WAMFFN_PAIR", true);
@@ -266,7 +301,10 @@ int default_splits(int n_out, int k_in, int sm_count) {
 }
 
 int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* weight, bool packed,
-                const void* act, const void* bias, void* out, unsigned int* status, bool pdl) {
+                const void* act, const void* bias, void* out, unsigned int* status, bool pdl,
+                float* sk_ws = nullptr, unsigned int* sk_flags = nullptr) {
+  if (c.sk > 0 && (epi == EPI_PARTIAL_F32 || !sk_ws || !sk_flags))
+    return fail(WAMFFN_ERR_INVALID, "stream-K needs a bias or GELU epilogue and its workspace");
   CUtensorMap tm_w, tm_x;
   int rc = packed ? encode_operand(&tm_w, weight, uint64_t(kBlockK), uint64_t(c.n_out) * (c.k_in / kBlockK),
                                    uint64_t(kBlockK) * 2, kFeatTile)
@@ -296,9 +334,14 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   p.bias = static_cast<const __nv_bfloat16*>(bias);
   p.out = out;
   p.status = status;
+  p.sk = c.sk;
+  p.sk_tiles = c.n_out / (kFeatTile * c.group);
+  p.sk_ws = sk_ws;
+  p.sk_flags = sk_flags;
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(unsigned(c.n_out / kFeatTile), unsigned(c.splits), unsigned(c.groups));
+  cfg.gridDim = c.sk > 0 ? dim3(unsigned(c.sk * c.group), 1, 1)
+                         : dim3(unsigned(c.n_out / kFeatTile), unsigned(c.splits), unsigned(c.groups));
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = size_t(c.smem_bytes);
   cfg.stream = stream;
@@ -311,8 +354,13 @@ int launch_gemm(const GemmConfig& c, int epi, cudaStream_t stream, const void* w
   attr[1].val.clusterDim.z = 1;  // token groups are independent: clusters of more than 2 CTAs fit fewer SMs
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (c.group == 2) WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<2>, tm_w, tm_x, p));
-  else WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<1>, tm_w, tm_x, p));
+  if (c.sk > 0) {
+    if (c.group == 2) WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<2, true>, tm_w, tm_x, p));
+    else WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<1, true>, tm_w, tm_x, p));
+  } else {
+    if (c.group == 2) WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<2, false>, tm_w, tm_x, p));
+    else WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, umma_gemm_kernel<1, false>, tm_w, tm_x, p));
+  }
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;
 }
@@ -373,6 +421,8 @@ struct wamffn_linear_plan {
   float* partial = nullptr;      // [splits, rows, n_out] when splits > 1
   __nv_bfloat16* hidden = nullptr;  // [rows, n_out] scratch for wamffn_ffn_run (up plans)
   unsigned int* status = nullptr;
+  float* sk_ws = nullptr;           // stream-K helper slots when cfg.sk > 0
+  unsigned int* sk_flags = nullptr;
 };
 
 struct wamffn_block_plan {
@@ -390,6 +440,9 @@ struct wamffn_block_plan {
   unsigned int* pass_bars = nullptr;  // phase counters of the persistent pass kernel
   int pass_ctas = 0;                  // co-resident CTAs of the pass kernel (0: unavailable)
   int split_override[kMaxTokens + 1];  // tuned split-K per row count (0 = heuristic)
+  int up_streamk = 1;                 // stream-K up projection when its tiles leave SMs idle
+  float* sk_ws = nullptr;             // stream-K helper slots of the up projection
+  unsigned int* sk_flags = nullptr;
 };
 
 namespace {
@@ -400,7 +453,7 @@ int linear_execute(wamffn_linear_plan* plan, cudaStream_t stream, const void* x,
   const bool pdl = pdl_enabled();
   if (c.splits == 1) {
     return launch_gemm(c, plan->gelu ? EPI_GELU_BF16 : EPI_BIAS_BF16, stream, weight, plan->packed, x, bias, out,
-                       plan->status, pdl);
+                       plan->status, pdl, plan->sk_ws, plan->sk_flags);
   }
   int rc = launch_gemm(c, EPI_PARTIAL_F32, stream, weight, plan->packed, x, nullptr, plan->partial, plan->status,
                        pdl);
@@ -485,6 +538,10 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
     delete plan;
     return rc;
   }
+  // Stream-K for a GELU plan whose tiles leave SMs idle (the split-K reduction
+  // of the bias plans fills the machine instead).
+  const int sk_candidate = (plan->gelu && streamk_enabled()) ? streamk_groups(plan->cfg, sm) : 0;
+  plan->cfg.sk = sk_candidate;
   auto cleanup = [&](int code) {
     wamffn_linear_plan_destroy(plan);
     return code;
@@ -494,6 +551,11 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
     return cleanup(fail(WAMFFN_ERR_CUDA, "status allocation failed"));
   if (plan->gelu && cudaMalloc(&plan->hidden, size_t(rows) * n_out * 2) != cudaSuccess)
     return cleanup(fail(WAMFFN_ERR_CUDA, "hidden scratch allocation failed"));
+  if (sk_candidate > 0 &&
+      (cudaMalloc(&plan->sk_ws, streamk_ws_bytes(sm, plan->cfg.tok_pad)) != cudaSuccess ||
+       cudaMalloc(&plan->sk_flags, size_t(sm) * sizeof(unsigned int)) != cudaSuccess ||
+       cudaMemset(plan->sk_flags, 0, size_t(sm) * sizeof(unsigned int)) != cudaSuccess))
+    return cleanup(fail(WAMFFN_ERR_CUDA, "stream-K workspace allocation failed"));
   const int tiles = n_out / kFeatTile;
   if (tune) {
     // Candidate split-K factors are timed on scratch operands, the way the
@@ -511,18 +573,26 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
       cudaMemset(w, 0x3c, size_t(n_out) * k_in * 2);
       cudaMemset(b, 0, size_t(n_out) * 2);
       float best = 1e30f;
-      int best_s = plan->cfg.splits;
+      int best_s = plan->cfg.splits, best_sk = 0;
       for (int s = 1; s <= max_s; ++s) {
-        GemmConfig c;
-        if (make_gemm_config(rows, n_out, k_in, s, &c)) continue;
-        plan->cfg = c;
-        float ms = 0;
-        if (time_linear(plan, x, w, b, o, &ms) == WAMFFN_OK && ms < best) {
-          best = ms;
-          best_s = s;
+        // Candidates: split-K factors, and for the GELU plan also the stream-K grid.
+        const int sks[2] = {0, sk_candidate};
+        const int n_sk = (s == 1 && sk_candidate > 0) ? 2 : 1;
+        for (int j = 0; j < n_sk; ++j) {
+          GemmConfig c;
+          if (make_gemm_config(rows, n_out, k_in, s, &c)) continue;
+          c.sk = sks[j];
+          plan->cfg = c;
+          float ms = 0;
+          if (time_linear(plan, x, w, b, o, &ms) == WAMFFN_OK && ms < best) {
+            best = ms;
+            best_s = s;
+            best_sk = sks[j];
+          }
         }
       }
       make_gemm_config(rows, n_out, k_in, best_s, &plan->cfg);
+      plan->cfg.sk = best_sk;
       plan->tuned = 1;
     }
     cudaFree(x);
@@ -547,6 +617,8 @@ int wamffn_linear_plan_destroy(wamffn_linear_plan* plan) {
   cudaFree(plan->partial);
   cudaFree(plan->hidden);
   cudaFree(plan->status);
+  cudaFree(plan->sk_ws);
+  cudaFree(plan->sk_flags);
   delete plan;
   return WAMFFN_OK;
 }
@@ -569,6 +641,7 @@ int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values
                          uint32_t(c.a_stages * 100 + c.b_stages), uint32_t(c.splits), c.tmem_cols,
                          uint32_t(plan->tuned)};
   for (int i = 0; i < n && i < 7; ++i) values[i] = v[i];
+  if (n > 7) values[7] = uint32_t(c.sk);  // stream-K CTA groups (0 = data-parallel grid)
   return WAMFFN_OK;
 }
 
@@ -769,6 +842,16 @@ int wamffn_block_plan_create(int device, int max_rows, int max_seq, int d_model,
             cudaMemset(plan->status, 0, sizeof(unsigned int)) == cudaSuccess &&
             cudaMalloc(&plan->pass_bars, (3 * kPassMaxLayers + 1) * sizeof(unsigned int)) == cudaSuccess;
   if (!ok) return cleanup(fail(WAMFFN_ERR_CUDA, "block plan allocation failed"));
+  plan->up_streamk = streamk_enabled() ? 1 : 0;
+  {
+    // Stream-K helper slots for the largest up projection this plan runs.
+    GemmConfig c;
+    make_gemm_config(max_rows, d_hidden, d_model, 1, &c);
+    ok = cudaMalloc(&plan->sk_ws, streamk_ws_bytes(sm, c.tok_pad)) == cudaSuccess &&
+         cudaMalloc(&plan->sk_flags, size_t(sm) * sizeof(unsigned int)) == cudaSuccess &&
+         cudaMemset(plan->sk_flags, 0, size_t(sm) * sizeof(unsigned int)) == cudaSuccess;
+    if (!ok) return cleanup(fail(WAMFFN_ERR_CUDA, "stream-K workspace allocation failed"));
+  }
   {
     // The pass kernel's grid barriers need every CTA resident at once: one CTA
     // per SM, in clusters of two.
@@ -803,6 +886,8 @@ int wamffn_block_plan_destroy(wamffn_block_plan* plan) {
   cudaFree(plan->pos);
   cudaFree(plan->status);
   cudaFree(plan->pass_bars);
+  cudaFree(plan->sk_ws);
+  cudaFree(plan->sk_flags);
   delete plan;
   return WAMFFN_OK;
 }
@@ -814,9 +899,11 @@ int env_int(const char* name, int dflt) {
 }
 
 int block_configs(const wamffn_block_plan* plan, int rows, GemmConfig* up, GemmConfig* down) {
-  // The up projection applies GELU in its epilogue: it never splits K.
+  // The up projection applies GELU in its epilogue: it never splits K; when
+  // its feature tiles leave SMs idle it runs as stream-K (on every SM).
   int rc = make_gemm_config(rows, plan->h, plan->d, 1, up);
   if (rc) return rc;
+  up->sk = plan->up_streamk ? streamk_groups(*up, plan->sm_count) : 0;
   // Down projection: K = h is long and the output narrow, so the SMs are filled
   // with split-K (optionally x token groups).
   // Token groups (grid.z) halve the partials but made the mainloop HBM-bound
@@ -899,7 +986,7 @@ int wamffn_block_run(wamffn_block_plan* plan, void* stream_, const wamffn_block_
   if (rc) return rc;
   // 2. up projection + bias + GELU -> hidden.
   rc = launch_gemm(up, EPI_GELU_BF16, stream, a->w_up, a->weights_packed != 0, plan->gathered, a->b_up,
-                   plan->hidden, plan->status, pdl);
+                   plan->hidden, plan->status, pdl, plan->sk_ws, plan->sk_flags);
   if (rc) return rc;
   // 3. down projection, split-K fp32 partials.
   rc = launch_gemm(down, EPI_PARTIAL_F32, stream, a->w_down, a->weights_packed != 0, plan->hidden, nullptr,
@@ -1144,7 +1231,7 @@ int stack_run_impl(wamffn_block_plan* plan, void* stream_, const wamffn_stack_ar
     rc = block_configs(plan, rows, &up, &down);
     if (rc) return rc;
     rc = launch_gemm(up, EPI_GELU_BF16, stream, w.w_up, a->weights_packed != 0, plan->gathered, w.b_up, plan->hidden,
-                     plan->status, pdl);
+                     plan->status, pdl, plan->sk_ws, plan->sk_flags);
     if (rc) return rc;
     // Unsplit K (concurrent lanes): the GEMM applies the bias and rounds to
     // bf16 itself, the boundary reads half the bytes.  Same values either way.
@@ -1269,6 +1356,15 @@ int wamffn_block_configuration(const wamffn_block_plan* plan, int rows, uint32_t
                            uint32_t(c->a_stages * 100 + c->b_stages), uint32_t(c->splits), c->tmem_cols, 0u};
     for (int i = 0; i < 7 && k < n; ++i) values[k++] = v[i];
   }
+  // Values 14 and 15: stream-K CTA groups of the up and down projections (0 = data-parallel grid).
+  for (const GemmConfig* c : cs)
+    if (k < n) values[k++] = uint32_t(c->sk);
+  return WAMFFN_OK;
+}
+
+int wamffn_block_plan_set_streamk(wamffn_block_plan* plan, int enabled) {
+  if (!plan) return fail(WAMFFN_ERR_INVALID, "null plan");
+  plan->up_streamk = enabled ? 1 : 0;
   return WAMFFN_OK;
 }
 

@@ -122,7 +122,7 @@ class FFNStack:
     """L fused FFN blocks over resident weights on one device."""
 
     def __init__(self, weights: list[LayerWeights], geo: Geometry, device, eps: float = 1e-6, lanes: int = 1,
-                 down_splits: int | None = None):
+                 down_splits: int | None = None, streamk: bool | None = None):
         from waminfer_b200.ffn import pack_weight
 
         if lanes < 1:
@@ -141,6 +141,8 @@ class FFNStack:
         if down_splits is not None:
             for plan in self.plans:
                 plan.set_splits(0, down_splits)
+        if streamk is not None:
+            self.set_streamk(streamk)
         self._streams = [torch.cuda.Stream(self.device) for _ in range(lanes)] if lanes > 1 else []
         self._pingpong = [torch.empty(geo.seq, geo.d, device=device, dtype=torch.bfloat16) for _ in range(2)]
         self._keep = []  # argument structs referenced by enqueued launches
@@ -235,6 +237,12 @@ class FFNStack:
         from now on (0: the SM-filling heuristic, best for one lane)."""
         for plan in self.plans:
             plan.set_splits(0, splits)
+
+    def set_streamk(self, enabled: bool) -> None:
+        """Stream-K up projection (every SM pair takes an equal share of the
+        feature tiles' K blocks) on every lane, for launches enqueued from now on."""
+        for plan in self.plans:
+            plan.set_streamk(enabled)
 
     def enqueue_requests(self, requests: list[Request], stream: int, lanes: int | None = None) -> None:
         """A batch of independent requests.  With one lane they run in order on
