@@ -314,3 +314,45 @@ def test_streamk_gelu_plans_follow_oracle(cuda_device, tmp_path):
     env = dict(os.environ, WAMFFN_STREAMK="1", PYTHONPATH=root)
     out = subprocess.run([sys.executable, str(script)], env=env, cwd=root, timeout=600, capture_output=True, text=True)
     assert out.returncode == 0, out.stdout + out.stderr
+
+
+def test_register_norm_is_bit_identical_to_row_kernel(cuda_device, tmp_path):
+    """The standalone op's register-resident kernel (4 warps per row) and the
+    shared-memory row kernel that the stack's first layer and the layer
+    boundary share compute the same bits, every mode, per-token and shared
+    time rows, strided inputs (WAMFFN_NORM_REG is read once per process, so
+    each kernel runs in its own child interpreter)."""
+    import os
+    import subprocess
+    import sys
+
+    script = tmp_path / "norm.py"
+    script.write_text(
+        "import sys, torch\n"
+        "from waminfer_b200.norm import modulated_norm\n"
+        "dev = torch.device('cuda', 0)\n"
+        "g = torch.Generator(device=dev).manual_seed(3)\n"
+        "out = {}\n"
+        "for dim, rows in ((3072, 392), (1024, 77), (256, 5)):\n"
+        "    r = lambda *s, std=1.0: (torch.randn(*s, device=dev, generator=g) * std).bfloat16()\n"
+        "    x = r(1, rows, dim + 8)[:, :, 8:]\n"
+        "    upd, mod, prev = r(1, rows, dim), r(1, 6, dim, std=0.1), r(1, 6, dim, std=0.1)\n"
+        "    w, b = r(dim, std=0.1), r(dim, std=0.1)\n"
+        "    for shared in (False, True):\n"
+        "        time = r(1, 1, 6, dim, std=0.1) if shared else r(1, rows, 6, dim, std=0.1)\n"
+        "        for mode in range(4):\n"
+        "            y, n = modulated_norm(x, upd if mode else None, mod, prev if mode == 3 else None, time,\n"
+        "                                  w if mode == 1 else None, b if mode == 1 else None, mode, 1e-6)\n"
+        "            out[(dim, shared, mode)] = (y.cpu(), n.cpu())\n"
+        "torch.save(out, sys.argv[1])\n")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    results = []
+    for flag in ("1", "0"):
+        env = dict(os.environ, WAMFFN_NORM_REG=flag, PYTHONPATH=root)
+        path = tmp_path / f"norm{flag}.pt"
+        subprocess.run([sys.executable, str(script), str(path)], check=True, env=env, cwd=root, timeout=600)
+        results.append(torch.load(path))
+    assert results[0].keys() == results[1].keys()
+    for key in results[0]:
+        for a, b in zip(results[0][key], results[1][key]):
+            assert torch.equal(a, b), key

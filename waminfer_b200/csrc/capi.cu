@@ -800,6 +800,23 @@ int wamffn_modulated_norm(void* stream, const wamffn_norm_args* a) {
   p.mode = a->mode;
   p.eps = a->eps;
   p.pdl = 1;
+  const int nvec = a->dim / 8;
+  static const bool reg = env_flag("WAMFFN_NORM_REG", true);
+  if (reg && nvec % 32 == 0 && nvec <= kRowThreads) {
+    // Register-resident variant (same bits as modnorm_kernel, 4 warps per row).
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(unsigned(a->rows), 1, 1);
+    cfg.blockDim = dim3(kNormRegThreads, 1, 1);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, modnorm_reg_kernel, p));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return WAMFFN_OK;
+  }
   return launch_norm(p, a->rows, static_cast<cudaStream_t>(stream), pdl_enabled());
 }
 

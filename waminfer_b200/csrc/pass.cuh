@@ -281,7 +281,7 @@ __device__ void pass_row(const PassParams& p, int l, int r, int et, float* red, 
       store8((has_next ? p.y : p.x_out) + size_t(row) * d + e, x);
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) local += x[i];
+    for (int i = 0; i < 8; ++i) local = __fadd_rn(local, x[i]);
   }
   if (!has_next) return;
 
@@ -299,7 +299,7 @@ __device__ void pass_row(const PassParams& p, int l, int r, int et, float* red, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float c = x[i] - mean;
-      local += c * c;
+      local = __fadd_rn(local, __fmul_rn(c, c));  // as the row kernels: no FMA
     }
   }
   const float var = pass_row_sum(local, red, nwarps) / float(d);

@@ -433,4 +433,36 @@ __device__ __forceinline__ float bf16_round(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// Packed bf16x2 arithmetic (two values per 32-bit register), each result the
+// correctly rounded bf16 of the exact sum / product.  For bf16 operands that
+// equals rounding the fp32 sum / product to bf16, which is how the reference
+// computes these steps: a product of two 8-bit significands is exact in fp32,
+// and an fp32 sum of two bf16 values is either exact (exponents within 16 of
+// each other) or off by less than 2^-16 of the larger operand, too little to
+// reach a bf16 rounding boundary.
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Two fp32 values rounded to bf16 and packed (lo in the low half).
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ float bf2_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf2_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+__device__ __forceinline__ uint4 bf2_add4(uint4 a, uint4 b) {
+  return make_uint4(bf2_add(a.x, b.x), bf2_add(a.y, b.y), bf2_add(a.z, b.z), bf2_add(a.w, b.w));
+}
+__device__ __forceinline__ uint4 bf2_mul4(uint4 a, uint4 b) {
+  return make_uint4(bf2_mul(a.x, b.x), bf2_mul(a.y, b.y), bf2_mul(a.z, b.z), bf2_mul(a.w, b.w));
+}
+
 }  // namespace wamffn

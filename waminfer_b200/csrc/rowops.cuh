@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(kRowThreads) modnorm_kernel(const NormParams p
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       xrow[e + i] = x[i];
-      local += x[i];
+      local = __fadd_rn(local, x[i]);
     }
     if (p.y != nullptr) store8(p.y + size_t(row) * p.dim + e, x);
   }
@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(kRowThreads) modnorm_kernel(const NormParams p
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float c = xrow[v * 8 + i] - mean;
-      local += c * c;
+      local = __fadd_rn(local, __fmul_rn(c, c));  // no FMA: the reference kernel runs without fp fusion
     }
   }
   const float var = block_sum(local, red) / float(p.dim);
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kRowThreads) modnorm_kernel(const NormParams p
       load8(p.weight + e, w);
       load8(p.bias + e, bb);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) n[i] = n[i] * w[i] + bb[i];
+      for (int i = 0; i < 8; ++i) n[i] = __fadd_rn(__fmul_rn(n[i], w[i]), bb[i]);
     } else {
       float shift[8], scale[8];
       modulation8(p.mod, p.time, p.ts, row, sh, p.dim, e, shift);
@@ -275,6 +275,148 @@ __global__ void __launch_bounds__(kRowThreads) modnorm_kernel(const NormParams p
     for (int k = 0; k < nm; ++k) store8(p.gathered + size_t(matches[k]) * p.dim + e, n);
   }
   if (tid == 0) pdl_launch_dependents();
+}
+
+// The standalone modulated norm (op wam_ffn::modulated_norm) with the row
+// held in registers: 4 warps per row, as the reference's Triton kernel runs
+// (_triton_inference.py:201-220), every load of the row issued before the
+// first reduction.  It computes the same bits as modnorm_kernel: the row
+// kernels' reduction order is that of 32-lane groups of consecutive 16-byte
+// vectors (a sequential sum of the vector's 8 values, a xor butterfly across
+// the group, the group sums added in order), and thread t here holds the
+// vectors t, t + 128 and t + 256, i.e. one lane of groups w, w + 4 and w + 8
+// (w = t / 32), so each group is reduced by one warp exactly as before.
+// For rows of nvec = dim / 8 vectors with nvec % 32 == 0 and nvec <= 384.
+constexpr int kNormRegThreads = 128;
+constexpr int kNormRegVecs = kRowThreads / kNormRegThreads;  // vectors per thread (3 at dim 3072)
+
+__device__ __forceinline__ void group_sums(float (&v)[kNormRegVecs], float* red, int groups) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kNormRegVecs; ++j) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v[j] = __fadd_rn(v[j], __shfl_xor_sync(0xffffffffu, v[j], o));
+    const int g = warp + j * (kNormRegThreads / 32);
+    if (lane == 0 && g < groups) red[g] = v[j];
+  }
+}
+
+__device__ __forceinline__ float ordered_total(const float* red, int groups) {
+  float s = 0.f;
+  for (int g = 0; g < groups; ++g) s = __fadd_rn(s, red[g]);
+  return s;
+}
+
+__global__ void __launch_bounds__(kNormRegThreads) modnorm_reg_kernel(const NormParams p) {
+  __shared__ float red[2][kRowThreads / 32];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int nvec = p.dim >> 3;
+  const int groups = nvec >> 5;
+  if (p.pdl) pdl_wait_prior();
+  if (tid == 0) pdl_launch_dependents();
+  const int mode = p.mode;
+  const bool residual = mode > 0 && p.update != nullptr;
+  const bool self_res = mode == WAMFFN_SELF_RESIDUAL;
+  const int gslot = self_res ? 2 : 5;                       // gate slot of the residual update
+  const __nv_bfloat16* gmod = self_res ? p.mod : p.previous;
+  const int sh = mode == WAMFFN_CROSS_RESIDUAL ? 3 : 0;
+  const int sc = mode == WAMFFN_CROSS_RESIDUAL ? 4 : 1;
+  const __nv_bfloat16* trow = p.time + size_t(row) * p.ts;
+
+  // Every load of the row first: x, the update and its gate, the shift and
+  // scale (or the affine weight and bias).
+  uint4 xv[kNormRegVecs], uv[kNormRegVecs], gm[kNormRegVecs], gt[kNormRegVecs];
+  uint4 am[kNormRegVecs], at[kNormRegVecs], bm[kNormRegVecs], bt[kNormRegVecs];
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int j = 0; j < kNormRegVecs; ++j) {
+    const int v = tid + j * kNormRegThreads;
+    const int e = v * 8;
+    xv[j] = uv[j] = gm[j] = gt[j] = am[j] = at[j] = bm[j] = bt[j] = zero;
+    if (v < nvec) {
+      xv[j] = *reinterpret_cast<const uint4*>(p.x + size_t(row) * p.xs + e);
+      if (residual) {
+        uv[j] = *reinterpret_cast<const uint4*>(p.update + size_t(row) * p.us + e);
+        if (self_res || mode == WAMFFN_FFN_RESIDUAL) {
+          gm[j] = *reinterpret_cast<const uint4*>(gmod + size_t(gslot) * p.dim + e);
+          gt[j] = *reinterpret_cast<const uint4*>(trow + size_t(gslot) * p.dim + e);
+        }
+      }
+      if (self_res) {
+        am[j] = *reinterpret_cast<const uint4*>(p.weight + e);
+        bm[j] = *reinterpret_cast<const uint4*>(p.bias + e);
+      } else {
+        am[j] = *reinterpret_cast<const uint4*>(p.mod + size_t(sh) * p.dim + e);
+        at[j] = *reinterpret_cast<const uint4*>(trow + size_t(sh) * p.dim + e);
+        bm[j] = *reinterpret_cast<const uint4*>(p.mod + size_t(sc) * p.dim + e);
+        bt[j] = *reinterpret_cast<const uint4*>(trow + size_t(sc) * p.dim + e);
+      }
+    }
+  }
+
+  // Residual update in packed bf16x2 (each step rounded as the reference
+  // rounds it) and the per-vector fp32 sums.
+  float x[kNormRegVecs][8], local[kNormRegVecs];
+#pragma unroll
+  for (int j = 0; j < kNormRegVecs; ++j) {
+    if (residual) {
+      uint4 u = uv[j];
+      if (self_res || mode == WAMFFN_FFN_RESIDUAL) u = bf2_mul4(bf2_add4(gm[j], gt[j]), u);
+      xv[j] = bf2_add4(xv[j], u);
+    }
+    unpack8(xv[j], x[j]);
+    local[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) local[j] = __fadd_rn(local[j], x[j][i]);
+    const int v = tid + j * kNormRegThreads;
+    if (v < nvec && p.y != nullptr) *reinterpret_cast<uint4*>(p.y + size_t(row) * p.dim + v * 8) = xv[j];
+  }
+  group_sums(local, red[0], groups);
+  __syncthreads();
+  const float mean = ordered_total(red[0], groups) / float(p.dim);
+#pragma unroll
+  for (int j = 0; j < kNormRegVecs; ++j) {
+    local[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float c = x[j][i] - mean;
+      local[j] = __fadd_rn(local[j], __fmul_rn(c, c));
+    }
+  }
+  group_sums(local, red[1], groups);
+  __syncthreads();
+  const float var = ordered_total(red[1], groups) / float(p.dim);
+  const float rstd = rsqrtf(var + p.eps);
+
+  const uint32_t one2 = 0x3f803f80u;  // bf16x2 {1, 1}
+#pragma unroll
+  for (int j = 0; j < kNormRegVecs; ++j) {
+    const int v = tid + j * kNormRegThreads;
+    if (v >= nvec) continue;
+    float n[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) n[i] = (x[j][i] - mean) * rstd;
+    uint4 out;
+    if (self_res) {
+      float a[8], b[8];
+      unpack8(am[j], a);
+      unpack8(bm[j], b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) n[i] = __fadd_rn(__fmul_rn(n[i], a[i]), b[i]);
+      out = make_uint4(bf2_pack(n[0], n[1]), bf2_pack(n[2], n[3]), bf2_pack(n[4], n[5]), bf2_pack(n[6], n[7]));
+    } else {
+      // bf16(bf16(n) * bf16(1 + bf16(mod + time))) + bf16(mod + time), stored as bf16.
+      const uint4 shift = bf2_add4(am[j], at[j]);
+      const uint4 scale = bf2_add4(bm[j], bt[j]);
+      const uint4 s1 = make_uint4(bf2_add(one2, scale.x), bf2_add(one2, scale.y), bf2_add(one2, scale.z),
+                                  bf2_add(one2, scale.w));
+      const uint4 nb = make_uint4(bf2_pack(n[0], n[1]), bf2_pack(n[2], n[3]), bf2_pack(n[4], n[5]),
+                                  bf2_pack(n[6], n[7]));
+      out = bf2_add4(bf2_mul4(nb, s1), shift);
+    }
+    if (p.norm != nullptr) *reinterpret_cast<uint4*>(p.norm + size_t(row) * p.dim + v * 8) = out;
+  }
 }
 
 // One CTA per sequence row.
@@ -515,7 +657,7 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
     for (int i = 0; i < 8; ++i) {
       x[i] = bf16_round(y[i] + bf16_round(g[i] * o[i]));
       xrow[e + i] = x[i];
-      local += x[i];
+      local = __fadd_rn(local, x[i]);
     }
     if (last) store8(p.x_final + size_t(row) * p.dim + e, x);
     else store8(p.y + size_t(row) * p.dim + e, x);
@@ -539,7 +681,7 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const float c = xrow[v * 8 + i] - mean;
-      local += c * c;
+      local = __fadd_rn(local, __fmul_rn(c, c));  // no FMA: the reference kernel runs without fp fusion
     }
   }
   const float var = block_sum(local, red) / float(p.dim);
