@@ -119,6 +119,26 @@ __device__ __forceinline__ uint4 modulation8_packed(const __nv_bfloat16* mod, co
   return u;
 }
 
+// bf16(mod[slot] + time[row, slot]) for 8 consecutive features, packed bf16x2.
+__device__ __forceinline__ uint4 modulation8_bf2(const __nv_bfloat16* mod, const __nv_bfloat16* time, long long ts,
+                                                 int row, int slot, int dim, int e) {
+  return bf2_add4(*reinterpret_cast<const uint4*>(mod + size_t(slot) * dim + e),
+                  *reinterpret_cast<const uint4*>(time + size_t(row) * ts + size_t(slot) * dim + e));
+}
+
+// adaLN of 8 normalised features, packed: bf16(bf16(n) * bf16(1 + scale)) + shift,
+// rounded to bf16 (_triton_inference.py:170-176), with n = (x - mean) * rstd in fp32.
+__device__ __forceinline__ uint4 adaln8_bf2(const float* x, float mean, float rstd, uint4 shift, uint4 scale) {
+  const uint32_t one2 = 0x3f803f80u;  // bf16x2 {1, 1}
+  float n[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) n[i] = (x[i] - mean) * rstd;
+  const uint4 nb = make_uint4(bf2_pack(n[0], n[1]), bf2_pack(n[2], n[3]), bf2_pack(n[4], n[5]), bf2_pack(n[6], n[7]));
+  const uint4 s1 = make_uint4(bf2_add(one2, scale.x), bf2_add(one2, scale.y), bf2_add(one2, scale.z),
+                              bf2_add(one2, scale.w));
+  return bf2_add4(bf2_mul4(nb, s1), shift);
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -611,10 +631,10 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
   for (int v = tid; v < nvec; v += blockDim.x) {
     const int e = v * 8;
     const uint4 y_packed = *reinterpret_cast<const uint4*>(p.y + size_t(row) * p.dim + e);
-    const uint4 g_packed = modulation8_packed(p.mod, p.time, p.ts, row, 5, p.dim, e);
-    float o[8];
+    const uint4 g_packed = modulation8_bf2(p.mod, p.time, p.ts, row, 5, p.dim, e);
+    uint4 o;  // bf16 FFN output of this row
     if (kOutBf16 && j >= 0) {
-      load8(reinterpret_cast<const __nv_bfloat16*>(p.partial) + size_t(j) * p.dim + e, o);
+      o = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.partial) + size_t(j) * p.dim + e);
     } else if (j >= 0) {
       const float* base = p.partial + size_t(j) * p.dim + e;
       const size_t split_stride = size_t(p.m) * p.dim;
@@ -641,26 +661,24 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
       }
       float bb[8];
       load8(p.bias + e, bb);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = bf16_round(acc[i] + bb[i]);
+      o = make_uint4(bf2_pack(acc[0] + bb[0], acc[1] + bb[1]), bf2_pack(acc[2] + bb[2], acc[3] + bb[3]),
+                     bf2_pack(acc[4] + bb[4], acc[5] + bb[5]), bf2_pack(acc[6] + bb[6], acc[7] + bb[7]));
     } else if (cached_row && p.cache_in != nullptr) {
-      load8(p.cache_in + size_t(row) * p.dim + e, o);
+      o = *reinterpret_cast<const uint4*>(p.cache_in + size_t(row) * p.dim + e);
     } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = 0.f;
+      o = make_uint4(0, 0, 0, 0);
     }
-    if (cached_row && p.cache_out != nullptr) store8(p.cache_out + size_t(row) * p.dim + e, o);
-    float g[8], x[8], y[8];
-    unpack8(g_packed, g);
-    unpack8(y_packed, y);
+    if (cached_row && p.cache_out != nullptr) *reinterpret_cast<uint4*>(p.cache_out + size_t(row) * p.dim + e) = o;
+    // x = bf16(y + bf16(gate * o)), packed (the same roundings as the fp32 form).
+    const uint4 xp = bf2_add4(y_packed, bf2_mul4(g_packed, o));
+    float x[8];
+    unpack8(xp, x);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      x[i] = bf16_round(y[i] + bf16_round(g[i] * o[i]));
       xrow[e + i] = x[i];
       local = __fadd_rn(local, x[i]);
     }
-    if (last) store8(p.x_final + size_t(row) * p.dim + e, x);
-    else store8(p.y + size_t(row) * p.dim + e, x);
+    *reinterpret_cast<uint4*>((last ? p.x_final : p.y) + size_t(row) * p.dim + e) = xp;
   }
   if (rec) rec[3] = rec[4] = globaltimer_ns();
   if (last) {
@@ -672,8 +690,8 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
   // The first vector's shift / scale loads overlap the two reductions.
   uint4 pre_shift = make_uint4(0, 0, 0, 0), pre_scale = make_uint4(0, 0, 0, 0);
   if (tid < nvec) {
-    pre_shift = modulation8_packed(p.next_mod, p.time, p.ts, row, 3, p.dim, tid * 8);
-    pre_scale = modulation8_packed(p.next_mod, p.time, p.ts, row, 4, p.dim, tid * 8);
+    pre_shift = modulation8_bf2(p.next_mod, p.time, p.ts, row, 3, p.dim, tid * 8);
+    pre_scale = modulation8_bf2(p.next_mod, p.time, p.ts, row, 4, p.dim, tid * 8);
   }
   const float mean = block_sum(local, red) / float(p.dim);
   local = 0.f;
@@ -689,20 +707,10 @@ __global__ void __launch_bounds__(kRowThreads, 3) boundary_kernel(const Boundary
   const int nm = n_match < kMaxMatches ? n_match : kMaxMatches;
   for (int v = tid; v < nvec; v += blockDim.x) {
     const int e = v * 8;
-    float n[8], shift[8], scale[8];
-    if (v == tid) {
-      unpack8(pre_shift, shift);
-      unpack8(pre_scale, scale);
-    } else {
-      modulation8(p.next_mod, p.time, p.ts, row, 3, p.dim, e, shift);
-      modulation8(p.next_mod, p.time, p.ts, row, 4, p.dim, e, scale);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float s1 = bf16_round(1.0f + scale[i]);
-      n[i] = bf16_round(bf16_round((xrow[e + i] - mean) * rstd) * s1) + shift[i];
-    }
-    for (int k = 0; k < nm; ++k) store8(p.next_gathered + size_t(matches[k]) * p.dim + e, n);
+    const uint4 shift = v == tid ? pre_shift : modulation8_bf2(p.next_mod, p.time, p.ts, row, 3, p.dim, e);
+    const uint4 scale = v == tid ? pre_scale : modulation8_bf2(p.next_mod, p.time, p.ts, row, 4, p.dim, e);
+    const uint4 n = adaln8_bf2(xrow + e, mean, rstd, shift, scale);
+    for (int k = 0; k < nm; ++k) *reinterpret_cast<uint4*>(p.next_gathered + size_t(matches[k]) * p.dim + e) = n;
   }
   if (rec) rec[5] = globaltimer_ns();
 }
