@@ -61,6 +61,10 @@ def parse():
     p.add_argument("--no-tp", action="store_true",
                    help="with --gpus N > 1, skip the tensor-parallel line reported beside the headline")
     p.add_argument("--tp-requests", type=int, default=4, help="requests per step of that tensor-parallel line")
+    p.add_argument("--only", choices=("norm", "projections", "dominant"),
+                   help="profiling aid: time one component on cuda:0 and print its JSON (no bench line): the "
+                        "modulated norm against the reference's Triton kernel, the attention projections against "
+                        "torch, or the up-projection GEMM alone")
     p.add_argument("--tp", action="store_true",
                    help="tensor-parallel mode: every request's FFN hidden dimension split across the --gpus ranks "
                         "(one all-reduce per layer, strong scaling); not the default bench line")
@@ -1049,8 +1053,27 @@ def run_tp(args, world, rank, local, requests: int | None = None, report: bool =
     return line
 
 
+def run_only(args):
+    from waminfer_b200.stack import Geometry
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    geo = Geometry(layers=args.layers)
+    if args.only == "norm":
+        out = norm_timings(device, geo, 50)
+    elif args.only == "projections":
+        out = projection_timings(device, geo, 20)
+    else:
+        pk, kind = peaks()
+        out = time_dominant_kernel(device, geo, pk)
+    print(json.dumps({"only": args.only, **out}), flush=True)
+
+
 def main():
     args = parse()
+    if args.only:
+        run_only(args)
+        return
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
