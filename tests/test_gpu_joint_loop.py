@@ -1,0 +1,210 @@
+"""GPU: this library's FFN inside the reference's own branch scheduler.
+
+The reference's ``ParallelJointLoop`` (WAMInfer/joint.py:24-156, imported
+unchanged from baseline/_ref) runs a synthetic OpenWAM-shaped model
+(``tests/joint_model.py``: 3 video blocks at d = 3072 / h = 14336, 3 action
+blocks of half the width, the reference's adapters, driver, Triton Q/K RMSNorm
++ RoPE, modulated norms and masked attention) for one request with 32-of-120
+token reuse.  The video FFN is installed the ways a WAMInfer maintainer can
+install it:
+
+* ``vb.ffn = waminfer_b200.ffn.PreparedFFN(vb)`` at the reference's own call
+  site (WAMInfer/runtime.py:45; ``VideoAdapter.ffn_at_layer_for_compile``
+  calls its ``forward``);
+* ``vb.ffn_at_layer_for_compile = VideoFFN(vb).ffn_at_layer_for_compile``,
+  the fused phase (norm-fed gather, both GEMMs, history scatter, gate);
+
+against the reference's own two FFN paths: its cuBLASLt ``PreparedFFN`` and its
+native ``Linear -> GELU -> Linear`` (``vb.ffn = None``).  Both of this
+library's installs must stay closer to the reference's cuBLASLt path than the
+reference's two paths are to each other (they differ by design: the native
+path rounds to bf16 before GELU), rows served from the history must be the
+same bits everywhere, the loop captured into one CUDA graph must replay
+deterministically and stay as close to the reference's graph-replayed loop,
+and a last test builds the loop as the reference does, with every phase under
+``torch.compile``.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import ffn as offn
+
+pytestmark = pytest.mark.gpu
+
+LAYERS = 3
+COUNT = 32  # refreshed current-frame rows: 32 + 240 future rows = 272 per gathered layer
+
+
+@pytest.fixture(scope="module")
+def model(cuda_device):
+    import joint_model
+
+    ref, reason = joint_model.reference()
+    if ref is None:
+        pytest.skip(reason)
+    m = joint_model.JointModel(ref, LAYERS, cuda_device, seed=7)
+    yield m
+    del m
+    torch.cuda.empty_cache()
+
+
+def _install(m, how):
+    """Puts one FFN implementation into the model's VideoAdapter; returns a closer."""
+    from waminfer_b200.blocks import VideoFFN
+    from waminfer_b200.ffn import PreparedFFN
+
+    m.vb.__dict__.pop("ffn_at_layer_for_compile", None)
+    m.vb.ffn = None
+    rows = (360, 360 - 120 + COUNT)
+    if how == "reference_prepared":
+        with torch.no_grad():
+            m.vb.ffn = m.ref.ffn.PreparedFFN(m.vb)
+            m.vb.ffn.prepare(rows=rows)
+        return m.vb.ffn.close
+    if how == "ours_prepared":
+        with torch.no_grad():
+            m.vb.ffn = PreparedFFN(m.vb)
+            m.vb.ffn.prepare(rows=rows)
+        return m.vb.ffn.close
+    if how == "ours_fused":
+        fused = VideoFFN(m.vb, max_rows=360, max_seq=360)
+        with torch.no_grad():
+            fused.prepare()
+        m.vb.ffn_at_layer_for_compile = fused.ffn_at_layer_for_compile
+        return fused.close
+    return lambda: None  # "native": the reference's Linear -> GELU -> Linear
+
+
+def _run(m, loop):
+    video, action = m.states(COUNT)
+    with torch.no_grad():
+        video, action = loop(video, action)
+    torch.cuda.synchronize()
+    return (video.hidden_states.clone(), action.x_action.clone(), torch.stack(video.extras["token_outputs"]).clone(),
+            video.extras["token_indices"].clone())
+
+
+def _stats(a, b):
+    err = (a.float() - b.float()).abs()
+    worst = int(err.argmax())
+    ref = b.float().flatten()[worst:worst + 1]
+    return {"max_abs": float(err.max()), "mean_rel": float(err.mean() / b.float().abs().mean()),
+            "worst_ulp": float(offn.bf16_ulp(ref)[0])}
+
+
+@pytest.fixture(scope="module")
+def eager_runs(model):
+    runs = {}
+    for how in ("reference_prepared", "native", "ours_prepared", "ours_fused"):
+        close = _install(model, how)
+        try:
+            runs[how] = _run(model, model.loop(compiled=False))
+        finally:
+            close()
+    _install(model, "native")
+    return runs
+
+
+def test_ours_within_the_references_own_spread(model, eager_runs):
+    base = eager_runs["reference_prepared"]
+    spread = [_stats(x, y) for x, y in zip(eager_runs["native"][:3], base[:3])]
+    for how in ("ours_prepared", "ours_fused"):
+        run = eager_runs[how]
+        assert torch.equal(run[3], base[3]), how  # select_tokens indices (the reference's own function)
+        for part, (ours, theirs, s_ref) in enumerate(zip(run[:3], base[:3], spread)):
+            s = _stats(ours, theirs)
+            print(how, ("video", "action", "history")[part], s, "reference native vs cuBLASLt:", s_ref)
+            assert s["mean_rel"] <= s_ref["mean_rel"], (how, part, s, s_ref)
+            assert s["max_abs"] <= s_ref["max_abs"] + 2 * max(s["worst_ulp"], s_ref["worst_ulp"]), (how, part, s, s_ref)
+    # History rows that were not refreshed are the previous request's, in every implementation.
+    kept = sorted(set(range(120)) - set(base[3][:COUNT].tolist()))
+    for how, run in eager_runs.items():
+        assert torch.equal(run[2][:, :, kept], model.history[:, :, kept]), how
+
+
+def _within(s, s_ref):
+    return s["mean_rel"] <= s_ref["mean_rel"] and s["max_abs"] <= s_ref["max_abs"] + 2 * max(s["worst_ulp"],
+                                                                                           s_ref["worst_ulp"])
+
+
+def _graph_run(model, how):
+    """The whole joint loop (both streams, every layer) captured into one
+    CUDA graph and replayed twice; returns both replays' outputs."""
+    close = _install(model, how)
+    try:
+        loop = model.loop(compiled=False)
+        video, action = model.states(COUNT)
+        # The graph's inputs: the loop replaces the states' tensors while it is
+        # captured, so these references keep the input memory alive.
+        inputs = (video.hidden_states, action.x_action)
+        with torch.no_grad():
+            loop(*model.states(COUNT))  # warm-up outside the capture
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                video, action = loop(video, action)
+        replays = []
+        for _ in range(2):
+            graph.replay()
+            torch.cuda.synchronize()
+            replays.append([t.clone() for t in (video.hidden_states, action.x_action,
+                                                 torch.stack(video.extras["token_outputs"]))])
+        graph.reset()
+        del inputs
+        return replays
+    finally:
+        close()
+        _install(model, "native")
+
+
+def test_graph_replay_of_the_reference_loop(model, eager_runs):
+    """The loop with this library's FFN, captured as one CUDA graph: every
+    replay gives the same bits, and they are the eager run's bits whenever
+    the reference's own loop (cuBLASLt FFN, the control) replays to its eager
+    bits; in any case the replay stays as close to the reference's replayed
+    loop as the reference's two FFN paths are to each other."""
+    spread = [_stats(x, y) for x, y in zip(eager_runs["native"][:3], eager_runs["reference_prepared"][:3])]
+    theirs = _graph_run(model, "reference_prepared")
+    for t0, t1 in zip(*theirs):
+        assert torch.equal(t0, t1)
+    control_exact = all(torch.equal(g, e) for g, e in zip(theirs[0], eager_runs["reference_prepared"][:3]))
+    print("control: the reference's loop replays its eager bits:", control_exact)
+    for how in ("ours_prepared", "ours_fused"):
+        ours = _graph_run(model, how)
+        for t0, t1 in zip(*ours):
+            assert torch.equal(t0, t1), how
+        for part, (a, b, e, s_ref) in enumerate(zip(ours[0], theirs[0], eager_runs[how][:3], spread)):
+            s = _stats(a, b)
+            print(how, "graph vs reference graph", ("video", "action", "history")[part], s,
+                  "graph vs own eager:", _stats(a, e))
+            assert _within(s, s_ref), (how, part, s, s_ref)
+            if control_exact:
+                assert torch.equal(a, e), (how, part)
+
+
+def test_compiled_reference_loop_with_our_ffn(model, eager_runs):
+    """The loop as the reference builds it (every phase under torch.compile,
+    fullgraph): this library's custom ops trace through Dynamo via their fake
+    implementations.  Inductor regenerates the reference's own code around the
+    FFN, so the compiled loop with this library's FFN is compared with the
+    compiled loop with the reference's cuBLASLt FFN, within the reference's
+    own spread."""
+    spread = [_stats(x, y) for x, y in zip(eager_runs["native"][:3], eager_runs["reference_prepared"][:3])]
+    runs = {}
+    for how in ("reference_prepared", "ours_prepared"):
+        close = _install(model, how)
+        try:
+            runs[how] = _run(model, model.loop(compiled=True))
+        finally:
+            close()
+            _install(model, "native")
+    ours, theirs = runs["ours_prepared"], runs["reference_prepared"]
+    assert torch.equal(ours[3], theirs[3])
+    for part, (a, b, s_ref) in enumerate(zip(ours[:3], theirs[:3], spread)):
+        s = _stats(a, b)
+        print("compiled: ours vs reference", ("video", "action", "history")[part], s,
+              "compiled vs eager (ours):", _stats(a, eager_runs["ours_prepared"][part]))
+        assert _within(s, s_ref), (part, s, s_ref)
