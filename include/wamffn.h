@@ -35,6 +35,8 @@
  *                                  WAMInfer/approximation.py:55-67
  *   wamffn_rgb_mandatory        <- the RGB change test of TokenReuse.begin
  *                                  WAMInfer/approximation.py:31-36
+ *   wamffn_masked_attention     <- op wam_infer::masked_attention_mask_tiles_v4
+ *                                  WAMInfer/_triton_attention.py:238-263
  */
 #ifndef WAMFFN_H
 #define WAMFFN_H
@@ -410,6 +412,47 @@ int wamffn_select_tokens(void* stream, const wamffn_select_args* args);
  * ---------------------------------------------------------------------- */
 int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int height, int width, int grid_h,
                          int grid_w, void* mandatory);
+
+/* ------------------------------------------------------------------------
+ * Masked multi-head attention (op wam_infer::masked_attention_mask_tiles_v4,
+ * WAMInfer/_triton_attention.py:18-145, 238-263):
+ *   out[b, q, h*128:(h+1)*128] = softmax over k of (q . k / sqrt(128), keys where
+ *   mask[b, h, q, k] is false at -inf) . v
+ * with the reference's arithmetic (exp2 of scores scaled by 128^-0.5 log2 e,
+ * probabilities rounded to bf16 before the value product, fp32 normaliser,
+ * all-masked rows output 0).  q: [batch, nq, heads*128] rows q_row_stride
+ * elements apart (batch stride == nq * row stride); k, v: [batch, nk, ...]
+ * likewise (v may use any strides); mask: bool bytes addressed
+ * b*mask_strides[0] + h*[1] + q*[2] + k*[3] (0 = broadcast), or NULL; out:
+ * [batch, nq, heads*128] contiguous.  v_transposed is caller-owned scratch of
+ * wamffn_attention_scratch_bytes() bytes (the values rearranged keys-major for
+ * the tensor-core product).  `status` (optional, 4-byte aligned device word)
+ * receives WAMFFN_DEV_* bits.  Head dim 128 only.
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_attention_args {
+  const void* q;
+  int64_t q_row_stride;
+  int64_t q_batch_stride;
+  const void* k;
+  int64_t k_row_stride;
+  int64_t k_batch_stride;
+  const void* v;
+  int64_t v_row_stride;
+  int64_t v_batch_stride;
+  const void* mask;
+  int64_t mask_strides[4];
+  void* out;
+  void* v_transposed;
+  uint32_t* status;
+  int batch;
+  int nq;
+  int nk;
+  int heads;
+  int head_dim;
+} wamffn_attention_args;
+
+int wamffn_attention_scratch_bytes(int batch, int heads, int nk, size_t* bytes);
+int wamffn_masked_attention(void* stream, const wamffn_attention_args* args);
 
 #ifdef __cplusplus
 }

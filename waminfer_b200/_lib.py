@@ -51,6 +51,8 @@ EXPORTED_SYMBOLS = (
     "wamffn_block_configuration",
     "wamffn_block_plan_set_splits",
     "wamffn_block_plan_set_streamk",
+    "wamffn_attention_scratch_bytes",
+    "wamffn_masked_attention",
     "wamffn_rgb_mandatory",
     "wamffn_select_tokens",
     "wamffn_pack_weight",
@@ -86,6 +88,32 @@ class NormArgs(ctypes.Structure):
         ("dim", ctypes.c_int),
         ("mode", ctypes.c_int),
         ("eps", ctypes.c_float),
+    ]
+
+
+class AttentionArgs(ctypes.Structure):
+    """Mirror of ``wamffn_attention_args``."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("q_row_stride", ctypes.c_int64),
+        ("q_batch_stride", ctypes.c_int64),
+        ("k", ctypes.c_void_p),
+        ("k_row_stride", ctypes.c_int64),
+        ("k_batch_stride", ctypes.c_int64),
+        ("v", ctypes.c_void_p),
+        ("v_row_stride", ctypes.c_int64),
+        ("v_batch_stride", ctypes.c_int64),
+        ("mask", ctypes.c_void_p),
+        ("mask_strides", ctypes.c_int64 * 4),
+        ("out", ctypes.c_void_p),
+        ("v_transposed", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("batch", ctypes.c_int),
+        ("nq", ctypes.c_int),
+        ("nk", ctypes.c_int),
+        ("heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
     ]
 
 
@@ -203,6 +231,8 @@ def _declare(lib):
     lib.wamffn_block_configuration.argtypes = [vp, i, u32p, i]
     lib.wamffn_block_plan_set_splits.argtypes = [vp, i, i]
     lib.wamffn_block_plan_set_streamk.argtypes = [vp, i]
+    lib.wamffn_attention_scratch_bytes.argtypes = [i, i, i, ctypes.POINTER(ctypes.c_size_t)]
+    lib.wamffn_masked_attention.argtypes = [vp, ctypes.POINTER(AttentionArgs)]
     lib.wamffn_rgb_mandatory.argtypes = [vp, vp, vp, i, i, i, i, vp]
     lib.wamffn_select_tokens.argtypes = [vp, ctypes.POINTER(SelectArgs)]
     lib.wamffn_pack_weight.argtypes = [vp, vp, vp, i, i]
