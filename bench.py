@@ -61,7 +61,7 @@ def parse():
     p.add_argument("--no-tp", action="store_true",
                    help="with --gpus N > 1, skip the tensor-parallel line reported beside the headline")
     p.add_argument("--tp-requests", type=int, default=4, help="requests per step of that tensor-parallel line")
-    p.add_argument("--only", choices=("norm", "projections", "dominant"),
+    p.add_argument("--only", choices=("norm", "projections", "dominant", "attention"),
                    help="profiling aid: time one component on cuda:0 and print its JSON (no bench line): the "
                         "modulated norm against the reference's Triton kernel, the attention projections against "
                         "torch, or the up-projection GEMM alone")
@@ -558,6 +558,49 @@ def norm_timings(device, geo, replays):
             t_ours = _graph_ms_per_replay(ours, device, replays) / n * 1e3
             t_ref = _graph_ms_per_replay(reference, device, replays) / n * 1e3
         out[name] = {"ours_us": t_ours, "reference_triton_us": t_ref, "speedup": t_ref / t_ours}
+    return out
+
+
+ATTENTION_SHAPES = {  # (nq, nk, masked, tail): the DiT's attention calls at the default request geometry
+    "joint_392x392": (392, 392, False, False),          # video + action self-attention (joint.py:55-87)
+    "video_context_360x512": (360, 512, True, False),   # video cross-attention (blocks.py:233-239)
+    "action_context_32x512": (32, 512, True, True),     # action cross-attention (blocks.py:135)
+    "future_context_240x513": (240, 513, True, True),   # updates 1-9: future rows, 513-token context
+}
+
+
+def attention_timings(device, replays, heads=24):
+    """This library's masked attention against the reference's Triton kernel
+    (baseline/_ref) on the DiT's attention shapes, 20 calls per graph replay on
+    seeded inputs (the text mask pads the last quarter of the context)."""
+    sys.path.insert(0, str(ROOT / "baseline"))
+    import reference_phase as rp
+    from waminfer_b200.attention import masked_attention
+
+    reference = None
+    if not rp.missing(cuda=True):
+        rp.import_reference(cuda=True)
+        from WAMInfer import _triton_attention
+
+        reference = _triton_attention.masked_attention
+    g = torch.Generator(device=device).manual_seed(3)
+    out = {}
+    for name, (nq, nk, masked, tail) in ATTENTION_SHAPES.items():
+        q, k, v = (torch.randn(1, n, heads * 128, device=device, generator=g).bfloat16() for n in (nq, nk, nk))
+        mask = None
+        if masked:
+            mask = torch.ones(1, 1, 1, nk, dtype=torch.bool, device=device)
+            mask[..., int(nk * 0.75):] = False
+        calls = 20
+        with torch.no_grad():
+            ours = _graph_ms_per_replay(lambda: [masked_attention(q, k, v, mask, heads, tail) for _ in range(calls)],
+                                        device, replays) / calls * 1e3
+            entry = {"ours_us": ours}
+            if reference is not None:
+                theirs = _graph_ms_per_replay(
+                    lambda: [reference(q, k, v, mask, heads, tail=tail) for _ in range(calls)], device, replays) / calls
+                entry.update(reference_triton_us=theirs * 1e3, speedup=theirs * 1e3 / ours)
+        out[name] = entry
     return out
 
 
@@ -1061,6 +1104,8 @@ def run_only(args):
     geo = Geometry(layers=args.layers)
     if args.only == "norm":
         out = norm_timings(device, geo, 50)
+    elif args.only == "attention":
+        out = attention_timings(device, 20)
     elif args.only == "projections":
         out = projection_timings(device, geo, 20)
     else:

@@ -422,12 +422,10 @@ int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int 
  * probabilities rounded to bf16 before the value product, fp32 normaliser,
  * all-masked rows output 0).  q: [batch, nq, heads*128] rows q_row_stride
  * elements apart (batch stride == nq * row stride); k, v: [batch, nk, ...]
- * likewise (v may use any strides); mask: bool bytes addressed
- * b*mask_strides[0] + h*[1] + q*[2] + k*[3] (0 = broadcast), or NULL; out:
- * [batch, nq, heads*128] contiguous.  v_transposed is caller-owned scratch of
- * wamffn_attention_scratch_bytes() bytes (the values rearranged keys-major for
- * the tensor-core product).  `status` (optional, 4-byte aligned device word)
- * receives WAMFFN_DEV_* bits.  Head dim 128 only.
+ * likewise; mask: bool bytes addressed b*mask_strides[0] + h*[1] + q*[2] +
+ * k*[3] (0 = broadcast), or NULL; out: [batch, nq, heads*128] contiguous.
+ * `status` (optional, 4-byte aligned device word) receives WAMFFN_DEV_* bits.
+ * Head dim 128 only.  No scratch: K and V rows are read as they lie.
  * ---------------------------------------------------------------------- */
 typedef struct wamffn_attention_args {
   const void* q;
@@ -442,7 +440,6 @@ typedef struct wamffn_attention_args {
   const void* mask;
   int64_t mask_strides[4];
   void* out;
-  void* v_transposed;
   uint32_t* status;
   int batch;
   int nq;
@@ -451,7 +448,6 @@ typedef struct wamffn_attention_args {
   int head_dim;
 } wamffn_attention_args;
 
-int wamffn_attention_scratch_bytes(int batch, int heads, int nk, size_t* bytes);
 int wamffn_masked_attention(void* stream, const wamffn_attention_args* args);
 
 #ifdef __cplusplus

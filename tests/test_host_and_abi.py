@@ -171,14 +171,10 @@ def test_attention_abi_rejects_before_launching():
     from waminfer_b200 import _lib
 
     lib = _lib.lib()
-    size = ctypes.c_size_t()
-    assert lib.wamffn_attention_scratch_bytes(1, 24, 392, ctypes.byref(size)) == 0
-    assert size.value == 24 * 128 * 448 * 2  # keys padded to 64
-    assert lib.wamffn_attention_scratch_bytes(0, 24, 392, ctypes.byref(size)) == 1
     fake = 256
     args = _lib.AttentionArgs(q=fake, q_row_stride=3072, q_batch_stride=3072 * 392, k=fake, k_row_stride=3072,
                               k_batch_stride=3072 * 392, v=fake, v_row_stride=3072, v_batch_stride=3072 * 392,
-                              out=fake, v_transposed=fake, batch=1, nq=392, nk=392, heads=24, head_dim=64)
+                              out=fake, batch=1, nq=392, nk=392, heads=24, head_dim=64)
     assert lib.wamffn_masked_attention(None, ctypes.byref(args)) == 3  # head_dim 64: unsupported
     args.head_dim = 128
     args.q_batch_stride = 3072 * 391  # rows not at one stride across batches

@@ -51,7 +51,6 @@ EXPORTED_SYMBOLS = (
     "wamffn_block_configuration",
     "wamffn_block_plan_set_splits",
     "wamffn_block_plan_set_streamk",
-    "wamffn_attention_scratch_bytes",
     "wamffn_masked_attention",
     "wamffn_rgb_mandatory",
     "wamffn_select_tokens",
@@ -107,7 +106,6 @@ class AttentionArgs(ctypes.Structure):
         ("mask", ctypes.c_void_p),
         ("mask_strides", ctypes.c_int64 * 4),
         ("out", ctypes.c_void_p),
-        ("v_transposed", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
         ("batch", ctypes.c_int),
         ("nq", ctypes.c_int),
@@ -231,7 +229,6 @@ def _declare(lib):
     lib.wamffn_block_configuration.argtypes = [vp, i, u32p, i]
     lib.wamffn_block_plan_set_splits.argtypes = [vp, i, i]
     lib.wamffn_block_plan_set_streamk.argtypes = [vp, i]
-    lib.wamffn_attention_scratch_bytes.argtypes = [i, i, i, ctypes.POINTER(ctypes.c_size_t)]
     lib.wamffn_masked_attention.argtypes = [vp, ctypes.POINTER(AttentionArgs)]
     lib.wamffn_rgb_mandatory.argtypes = [vp, vp, vp, i, i, i, i, vp]
     lib.wamffn_select_tokens.argtypes = [vp, ctypes.POINTER(SelectArgs)]

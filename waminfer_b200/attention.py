@@ -43,9 +43,7 @@ def masked_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: to
         raise ValueError("q, k and v must be bf16")
     if not (q.is_cuda and k.is_cuda and v.is_cuda):
         raise ValueError("q, k and v must be CUDA tensors")
-    q, k = _rows(q, "q"), _rows(k, "k")
-    if v.stride(2) != 1 or v.data_ptr() % 16:
-        v = v.contiguous()
+    q, k, v = _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
     strides = (0, 0, 0, 0)
     if mask is not None:
         if mask.dtype != torch.bool:
@@ -53,15 +51,12 @@ def masked_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: to
         mask = torch.broadcast_to(mask, (batch, heads, nq, nk))
         strides = mask.stride()
     out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    need = ctypes.c_size_t()
-    _lib.check(_lib.lib().wamffn_attention_scratch_bytes(batch, heads, nk, ctypes.byref(need)))
-    scratch = torch.empty(need.value // 2, dtype=torch.bfloat16, device=q.device)
     args = _lib.AttentionArgs(
         q=q.data_ptr(), q_row_stride=q.stride(1), q_batch_stride=q.stride(0),
         k=k.data_ptr(), k_row_stride=k.stride(1), k_batch_stride=k.stride(0),
         v=v.data_ptr(), v_row_stride=v.stride(1), v_batch_stride=v.stride(0),
         mask=None if mask is None else mask.data_ptr(), mask_strides=(ctypes.c_int64 * 4)(*strides),
-        out=out.data_ptr(), v_transposed=scratch.data_ptr(), status=None,
+        out=out.data_ptr(), status=None,
         batch=batch, nq=nq, nk=nk, heads=heads, head_dim=HEAD_DIM)
     with torch.cuda.device(q.device):
         stream = torch.cuda.current_stream(q.device).cuda_stream

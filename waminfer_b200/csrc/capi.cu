@@ -13,8 +13,8 @@
 #include <string>
 #include <vector>
 
-#include "attention.cuh"
 #include "gemm.cuh"
+#include "attention.cuh"
 #include "pass.cuh"
 #include "rowops.cuh"
 #include "select.cuh"
@@ -1476,57 +1476,42 @@ int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int 
   return WAMFFN_OK;
 }
 
-int wamffn_attention_scratch_bytes(int batch, int heads, int nk, size_t* bytes) {
-  if (!bytes || batch < 1 || heads < 1 || nk < 1) return fail(WAMFFN_ERR_INVALID, "bad attention geometry");
-  const size_t nk_pad = size_t((nk + 63) / 64) * 64;
-  *bytes = size_t(batch) * heads * kAttnHeadDim * nk_pad * 2;
-  return WAMFFN_OK;
-}
-
 int wamffn_masked_attention(void* stream_, const wamffn_attention_args* a) {
   if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
   if (a->head_dim != kAttnHeadDim)
     return fail(WAMFFN_ERR_UNSUPPORTED, "head_dim=%d: the kernel runs D = %d", a->head_dim, kAttnHeadDim);
   if (a->batch < 1 || a->nq < 1 || a->nk < 1 || a->heads < 1 || a->batch > 65535 || a->heads > 65535)
     return fail(WAMFFN_ERR_INVALID, "batch=%d nq=%d nk=%d heads=%d", a->batch, a->nq, a->nk, a->heads);
-  if (!a->q || !a->k || !a->v || !a->out || !a->v_transposed) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
-  const void* ptrs[] = {a->q, a->k, a->v, a->out, a->v_transposed};
+  if (!a->q || !a->k || !a->v || !a->out) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
+  const void* ptrs[] = {a->q, a->k, a->v, a->out};
   for (const void* p : ptrs)
     if (!aligned16(p)) return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
   const int64_t width = int64_t(a->heads) * kAttnHeadDim;
-  // Rows of every batch must sit at one stride (a 2-D tensor map over batch x rows).
-  if (a->q_row_stride < width || a->q_row_stride % 8 || a->q_batch_stride != a->q_row_stride * a->nq)
-    return fail(WAMFFN_ERR_INVALID, "q strides (%lld, %lld): rows must be uniform, >= heads*128, multiples of 8",
-                (long long)a->q_batch_stride, (long long)a->q_row_stride);
-  if (a->k_row_stride < width || a->k_row_stride % 8 || a->k_batch_stride != a->k_row_stride * a->nk)
-    return fail(WAMFFN_ERR_INVALID, "k strides (%lld, %lld): rows must be uniform, >= heads*128, multiples of 8",
-                (long long)a->k_batch_stride, (long long)a->k_row_stride);
-  if (a->v_row_stride < width || a->v_batch_stride < a->v_row_stride * a->nk)
-    return fail(WAMFFN_ERR_INVALID, "v strides (%lld, %lld) too small", (long long)a->v_batch_stride,
-                (long long)a->v_row_stride);
+  // Rows of every batch at one stride (2-D tensor maps over batch x rows).
+  const struct { const char* name; int64_t row, batch; int rows; } views[3] = {
+      {"q", a->q_row_stride, a->q_batch_stride, a->nq},
+      {"k", a->k_row_stride, a->k_batch_stride, a->nk},
+      {"v", a->v_row_stride, a->v_batch_stride, a->nk}};
+  for (const auto& v : views)
+    if (v.row < width || v.row % 8 || v.batch != v.row * v.rows)
+      return fail(WAMFFN_ERR_INVALID,
+                  "%s strides (%lld, %lld): rows must sit at one stride across batches, >= heads*128, a multiple "
+                  "of 8 elements",
+                  v.name, (long long)v.batch, (long long)v.row);
   int dev = 0, sm = 0;
   WAMFFN_CUDA(cudaGetDevice(&dev));
   int rc = prepare_device(dev, &sm);
   if (rc) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  const int nk_pad = (a->nk + 63) / 64 * 64;
-  __nv_bfloat16* vt = static_cast<__nv_bfloat16*>(a->v_transposed);
-  {
-    dim3 grid(unsigned(nk_pad / 32), unsigned(kAttnHeadDim / 32), unsigned(a->batch * a->heads));
-    transpose_values_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<const __nv_bfloat16*>(a->v), a->v_row_stride,
-                                                             a->v_batch_stride, vt, a->heads, a->nk, nk_pad);
-    WAMFFN_CUDA(cudaGetLastError());
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-  }
-  CUtensorMap tm_q, tm_k, tm_vt;
+  CUtensorMap tm_q, tm_k, tm_v;
   rc = encode_operand(&tm_q, a->q, uint64_t(width), uint64_t(a->batch) * a->nq, uint64_t(a->q_row_stride) * 2,
                       kAttnRows);
   if (rc) return rc;
   rc = encode_operand(&tm_k, a->k, uint64_t(width), uint64_t(a->batch) * a->nk, uint64_t(a->k_row_stride) * 2,
                       kAttnKeys);
   if (rc) return rc;
-  rc = encode_operand(&tm_vt, vt, uint64_t(nk_pad), uint64_t(a->batch) * a->heads * kAttnHeadDim,
-                      uint64_t(nk_pad) * 2, kAttnHeadDim);
+  rc = encode_operand(&tm_v, a->v, uint64_t(width), uint64_t(a->batch) * a->nk, uint64_t(a->v_row_stride) * 2,
+                      kAttnKeys);
   if (rc) return rc;
   AttnParams p{};
   p.mask = static_cast<const unsigned char*>(a->mask);
@@ -1541,8 +1526,11 @@ int wamffn_masked_attention(void* stream_, const wamffn_attention_args* a) {
   p.batch = a->batch;
   p.scale_log2 = float((1.0 / sqrt(double(kAttnHeadDim))) * 1.4426950408889634);
   p.status = static_cast<unsigned int*>(a->status);
+  static const int vdesc = env_int("WAMFFN_ATTN_VDESC", 0);
+  p.v_lbo = vdesc ? kVGroupBytes : kVHalfBytes;
+  p.v_sbo = vdesc ? kVHalfBytes : kVGroupBytes;
   dim3 grid(unsigned((a->nq + kAttnRows - 1) / kAttnRows), unsigned(a->heads), unsigned(a->batch));
-  masked_attention_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tm_q, tm_k, tm_vt, p);
+  masked_attention_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tm_q, tm_k, tm_v, p);
   WAMFFN_CUDA(cudaGetLastError());
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;

@@ -123,6 +123,25 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
   }
 }
 
+// The same bounded wait as a pure spin on mbarrier.test_wait: no suspension,
+// so a phase that completes is seen within a few cycles.  For the short,
+// latency-critical handoffs of a serial pipeline (the attention kernel's
+// per-block chain), where a suspended waiter's wake-up would add up.
+__device__ __forceinline__ bool wait_spin(uint32_t bar, uint32_t parity, volatile int* abort, unsigned int* status,
+                                          unsigned int timeout_bit) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (*abort) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort = 1;
+      if (status) atomicOr(status, timeout_bit);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Same wait without the abort shortcut, used to drain in-flight copies.
 __device__ __forceinline__ bool wait_drain(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();
