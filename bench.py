@@ -596,11 +596,47 @@ def attention_timings(device, replays, heads=24):
             ours = _graph_ms_per_replay(lambda: [masked_attention(q, k, v, mask, heads, tail) for _ in range(calls)],
                                         device, replays) / calls * 1e3
             entry = {"ours_us": ours}
+            # The same call at each forced key split (CTAs per query tile).
+            entry["key_split_us"] = {
+                str(split): _graph_ms_per_replay(
+                    lambda: [masked_attention(q, k, v, mask, heads, tail, split) for _ in range(calls)], device,
+                    replays) / calls * 1e3 for split in (1, 2, 4)}
             if reference is not None:
                 theirs = _graph_ms_per_replay(
                     lambda: [reference(q, k, v, mask, heads, tail=tail) for _ in range(calls)], device, replays) / calls
                 entry.update(reference_triton_us=theirs * 1e3, speedup=theirs * 1e3 / ours)
         out[name] = entry
+    # The joint loop's structured layouts (joint.py:55-87): first-frame-causal
+    # self-attention over 360 video + 32 action rows (first frame 120 rows),
+    # and the current-frame step against a cached 120-row first frame.
+    from waminfer_b200.attention import current_frame_attention, joint_first_frame_attention
+
+    def rnd(rows):
+        return torch.randn(1, rows, heads * 128, device=device, generator=g).bfloat16()
+
+    q, k, v = rnd(392), rnd(392), rnd(392)
+    calls = 20
+    with torch.no_grad():
+        ours = _graph_ms_per_replay(lambda: [joint_first_frame_attention(q, k, v, 360, 120, heads)
+                                             for _ in range(calls)], device, replays) / calls * 1e3
+        entry = {"ours_us": ours}
+        if reference is not None:
+            ref_joint = _triton_attention.joint_first_frame_attention
+            theirs = _graph_ms_per_replay(lambda: [ref_joint(q, k, v, 360, 120, heads) for _ in range(calls)],
+                                          device, replays) / calls * 1e3
+            entry.update(reference_triton_us=theirs, speedup=theirs / ours)
+        out["joint_first_frame_392"] = entry
+        seg = dict(qv=rnd(240), qa=rnd(32), ck=rnd(120), kv=rnd(240), ka=rnd(32), cv=rnd(120), vv=rnd(240),
+                   va=rnd(32))
+        ours = _graph_ms_per_replay(lambda: [current_frame_attention(**seg, heads=heads) for _ in range(calls)],
+                                    device, replays) / calls * 1e3
+        entry = {"ours_us": ours}
+        if reference is not None:
+            ref_current = _triton_attention.current_frame_attention
+            theirs = _graph_ms_per_replay(lambda: [ref_current(**seg, heads=heads) for _ in range(calls)], device,
+                                          replays) / calls * 1e3
+            entry.update(reference_triton_us=theirs, speedup=theirs / ours)
+        out["current_frame_120+240+32"] = entry
     return out
 
 

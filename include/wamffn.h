@@ -37,6 +37,10 @@
  *                                  WAMInfer/approximation.py:31-36
  *   wamffn_masked_attention     <- op wam_infer::masked_attention_mask_tiles_v4
  *                                  WAMInfer/_triton_attention.py:238-263
+ *   wamffn_joint_first_frame_attention <- op wam_infer::joint_first_frame_attention_v2
+ *                                  WAMInfer/_triton_attention.py:327-334
+ *   wamffn_current_frame_attention <- op wam_infer::current_frame_attention_v1
+ *                                  WAMInfer/_triton_attention.py:429-484
  */
 #ifndef WAMFFN_H
 #define WAMFFN_H
@@ -48,7 +52,7 @@
 extern "C" {
 #endif
 
-#define WAMFFN_ABI_VERSION 1
+#define WAMFFN_ABI_VERSION 2
 
 /* Status codes returned by every entry point. */
 #define WAMFFN_OK 0
@@ -426,6 +430,10 @@ int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int 
  * k*[3] (0 = broadcast), or NULL; out: [batch, nq, heads*128] contiguous.
  * `status` (optional, 4-byte aligned device word) receives WAMFFN_DEV_* bits.
  * Head dim 128 only.  No scratch: K and V rows are read as they lie.
+ * key_split: 0 picks the split of the keys across a cluster of CTAs per query
+ * tile (1, 2 or 4: the largest that keeps the grid within one wave of SMs);
+ * 1, 2 or 4 forces it (halved while it exceeds the 128-key blocks).  The split
+ * moves the probabilities' bf16 rounding point, not the function.
  * ---------------------------------------------------------------------- */
 typedef struct wamffn_attention_args {
   const void* q;
@@ -446,9 +454,67 @@ typedef struct wamffn_attention_args {
   int nk;
   int heads;
   int head_dim;
+  int key_split;
 } wamffn_attention_args;
 
 int wamffn_masked_attention(void* stream, const wamffn_attention_args* args);
+
+/* One [batch, rows, heads*128] bf16 operand: rows row_stride elements apart,
+ * batch_stride == rows * row_stride (a multiple of 8 elements, 16-byte aligned). */
+typedef struct wamffn_rows_view {
+  const void* data;
+  int64_t row_stride;
+  int64_t batch_stride;
+} wamffn_rows_view;
+
+/* ------------------------------------------------------------------------
+ * Joint first-frame-causal attention (op wam_infer::joint_first_frame_attention_v2,
+ * WAMInfer/_triton_attention.py:267-334): q, k, v [batch, count, heads*128]
+ * (video rows then action rows); query rows [0, first) attend keys [0, first)
+ * (the clean first frame sees neither the future video nor the action rows),
+ * rows [first, count) attend all count keys.  out [batch, count, heads*128]
+ * contiguous.  `video` (the video row count) is carried for the reference's
+ * signature and changes nothing.  Arithmetic and key_split as
+ * wamffn_masked_attention.
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_joint_attention_args {
+  wamffn_rows_view q, k, v;
+  void* out;
+  uint32_t* status;
+  int batch;
+  int count;
+  int video;
+  int first;
+  int heads;
+  int head_dim;
+  int key_split;
+} wamffn_joint_attention_args;
+
+int wamffn_joint_first_frame_attention(void* stream, const wamffn_joint_attention_args* args);
+
+/* ------------------------------------------------------------------------
+ * Current-frame attention over a cached prefix (op wam_infer::current_frame_attention_v1,
+ * WAMInfer/_triton_attention.py:337-484): queries qv [batch, nv, .] then
+ * qa [batch, na, .] attend the keys ck [nc] ++ kv [nv] ++ ka [na] with values
+ * cv ++ vv ++ va, unmasked, without concatenating anything; outputs
+ * ov [batch, nv, heads*128] and oa [batch, na, heads*128], contiguous.
+ * Arithmetic and key_split as wamffn_masked_attention.
+ * ---------------------------------------------------------------------- */
+typedef struct wamffn_current_frame_args {
+  wamffn_rows_view qv, qa, ck, kv, ka, cv, vv, va;
+  void* ov;
+  void* oa;
+  uint32_t* status;
+  int batch;
+  int nc;
+  int nv;
+  int na;
+  int heads;
+  int head_dim;
+  int key_split;
+} wamffn_current_frame_args;
+
+int wamffn_current_frame_attention(void* stream, const wamffn_current_frame_args* args);
 
 #ifdef __cplusplus
 }

@@ -1,4 +1,8 @@
-"""torch-fp32 restatement of the reference's masked attention (test infrastructure only).
+"""torch-fp32 restatement of the reference's attention ops (test infrastructure only).
+
+``masked_attention`` restates the masked op; ``joint_first_frame_attention``
+and ``current_frame_attention`` restate the other two layouts as that
+function over a built mask / the concatenated segments.
 
 Follows ``_attention_kernel`` (WAMInfer/_triton_attention.py:18-107): scores
 ``q . k`` scaled by D^-0.5 log2(e); masked keys at -inf; exp2 against the row
@@ -35,3 +39,23 @@ def masked_attention(q, k, v, mask, heads: int) -> torch.Tensor:
     norm = p.sum(-1, keepdim=True)
     out = (p.to(torch.bfloat16).float() @ vh) / torch.where(norm > 0, norm, torch.ones_like(norm))
     return out.transpose(1, 2).reshape(b, nq, hidden)
+
+
+def joint_first_frame_attention(q, k, v, first: int, heads: int) -> torch.Tensor:
+    """``_joint_attention`` (WAMInfer/_triton_attention.py:267-313): rows
+    [0, first) attend keys [0, first), rows [first, count) attend every key.
+    fp32 [B, count, H*D]."""
+    count = q.shape[1]
+    rows = torch.arange(count, device=q.device)[:, None]
+    keys = torch.arange(count, device=q.device)[None, :]
+    mask = keys < torch.where(rows < first, first, count)
+    return masked_attention(q, k, v, mask, heads)
+
+
+def current_frame_attention(qv, qa, ck, kv, ka, cv, vv, va, heads: int):
+    """``_split_attention_kernel`` (WAMInfer/_triton_attention.py:337-426): the
+    queries qv ++ qa against the keys ck ++ kv ++ ka (values cv ++ vv ++ va),
+    unmasked; returns fp32 (ov, oa)."""
+    out = masked_attention(torch.cat((qv, qa), 1), torch.cat((ck, kv, ka), 1), torch.cat((cv, vv, va), 1), None,
+                           heads)
+    return out[:, :qv.shape[1]], out[:, qv.shape[1]:]

@@ -69,7 +69,7 @@ int main(void) {
   for (int i = 0; i < D * H; ++i) w_down[i] = to_bf16(0.05f * gauss());
   for (int i = 0; i < D; ++i) b_down[i] = to_bf16(0.01f * gauss());
 
-  if (wamffn_abi_version() != 1) {
+  if (wamffn_abi_version() != WAMFFN_ABI_VERSION) {
     fprintf(stderr, "unexpected ABI version %d\n", wamffn_abi_version());
     return 1;
   }

@@ -18,7 +18,7 @@ from oracle import ffn as offn
 pytestmark = pytest.mark.gpu
 
 
-def _reference_triton():
+def _reference_triton(name="masked_attention"):
     import sys
     from pathlib import Path
 
@@ -30,7 +30,7 @@ def _reference_triton():
     rp.import_reference(cuda=True)
     from WAMInfer import _triton_attention
 
-    return _triton_attention.masked_attention
+    return getattr(_triton_attention, name)
 
 
 def _case(dev, seed, b, nq, nk, heads, mask_kind):
@@ -94,3 +94,126 @@ def test_masked_attention_strided_query_from_packed_projection(cuda_device):
     assert torch.equal(out, dense)
     ok, msg = offn.check_close(out, oattn.masked_attention(q, k, v, None, 24))
     assert ok, msg
+
+
+@pytest.mark.parametrize("b,nq,nk,heads,mask_kind", [
+    (1, 32, 512, 24, "context"),  # the action rows: four key blocks
+    (1, 200, 520, 2, "random"),   # five key blocks: ranges of 1, 1, 1, 2 at split 4
+    (2, 129, 130, 3, "random"),   # two key blocks: split 4 runs as 2
+])
+def test_key_split_matches_the_oracle(cuda_device, b, nq, nk, heads, mask_kind):
+    """Every key split (one CTA per query tile, or 2 / 4 CTAs of a cluster
+    combining their partial results) against the oracle, and the splits
+    against each other within the same bf16-output rule."""
+    from waminfer_b200.attention import masked_attention
+
+    q, k, v, mask = _case(cuda_device, nq * 11 + nk, b, nq, nk, heads, mask_kind)
+    ref = oattn.masked_attention(q, k, v, mask, heads)
+    outs = {}
+    for split in (1, 2, 4):
+        outs[split] = masked_attention(q, k, v, mask, heads, False, split)
+        torch.cuda.synchronize()
+        ok, msg = offn.check_close(outs[split], ref)
+        print("split", split, (b, nq, nk, heads, mask_kind), msg)
+        assert ok, (split, msg)
+        if mask_kind == "random":
+            assert torch.count_nonzero(outs[split].view(b, nq, heads, 128)[:, 0]) == 0
+    for split in (2, 4):
+        ok, msg = offn.check_close(outs[split], outs[1].float())
+        assert ok, (split, msg)
+    again = masked_attention(q, k, v, mask, heads, False, 4)
+    assert torch.equal(again, outs[4])  # the combine sums in rank order: deterministic
+
+
+def _rand(dev, g, b, rows, heads):
+    return torch.randn(b, rows, heads * 128, device=dev, generator=g).bfloat16()
+
+
+@pytest.mark.parametrize("b,count,first,heads", [
+    (1, 392, 120, 24),  # the joint step: 3 frames of 120 video rows + 32 action rows, clean first frame
+    (2, 200, 64, 2),
+    (1, 150, 0, 2),     # no clean frame: every row sees every key
+    (1, 130, 130, 3),   # every row clean
+])
+def test_joint_first_frame_attention(cuda_device, b, count, first, heads):
+    """The joint first-frame-causal layout (op joint_first_frame_attention_v2)
+    against the oracle and the reference's Triton kernel, at every key split."""
+    from waminfer_b200.attention import joint_first_frame_attention
+
+    g = torch.Generator(device=cuda_device).manual_seed(count + first)
+    q, k, v = (_rand(cuda_device, g, b, count, heads) for _ in range(3))
+    ref = oattn.joint_first_frame_attention(q, k, v, first, heads)
+    triton = _reference_triton("joint_first_frame_attention")
+    theirs = triton(q, k, v, count - 32, first, heads).float() if triton is not None else None
+    for split in (0, 1, 2, 4):
+        out = joint_first_frame_attention(q, k, v, count - 32, first, heads, split)
+        torch.cuda.synchronize()
+        ok, msg = offn.check_close(out, ref)
+        print("joint", (b, count, first, heads), "split", split, "oracle", msg)
+        assert ok, (split, msg)
+        if theirs is not None:
+            ok, msg = offn.check_close(out, theirs)
+            assert ok, (split, "reference Triton", msg)
+
+
+@pytest.mark.parametrize("b,nc,nv,na,heads", [
+    (1, 120, 240, 32, 24),  # cached first frame, two future frames, the action rows
+    (2, 7, 50, 3, 2),       # ragged: every segment ends inside a key block
+    (1, 0, 130, 5, 2),      # no cached prefix
+    (1, 300, 1, 1, 2),
+])
+def test_current_frame_attention(cuda_device, b, nc, nv, na, heads):
+    """The cached-prefix layout (op current_frame_attention_v1): queries from
+    two tensors against keys / values from three, nothing concatenated,
+    against the oracle and the reference's Triton kernel, at every key split;
+    strided views of packed projections are taken as they lie."""
+    from waminfer_b200.attention import current_frame_attention
+
+    g = torch.Generator(device=cuda_device).manual_seed(nc * 3 + nv + na)
+    w = heads * 128
+    packed_v = _rand(cuda_device, g, b, nv, 3 * heads)  # video q / k / v from one packed projection
+    qv, kv, vv = packed_v[..., :w], packed_v[..., w:2 * w], packed_v[..., 2 * w:]
+    qa, ka, va = (_rand(cuda_device, g, b, na, heads) for _ in range(3))
+    ck, cv = _rand(cuda_device, g, b, nc, heads), _rand(cuda_device, g, b, nc, heads)
+    ref_v, ref_a = oattn.current_frame_attention(qv, qa, ck, kv, ka, cv, vv, va, heads)
+    triton = _reference_triton("current_frame_attention")
+    theirs = triton(qv, qa, ck, kv, ka, cv, vv, va, heads) if triton is not None else None
+    for split in (0, 1, 2, 4):
+        ov, oa = current_frame_attention(qv, qa, ck, kv, ka, cv, vv, va, heads, split)
+        torch.cuda.synchronize()
+        for name, got, exp, i in (("video", ov, ref_v, 0), ("action", oa, ref_a, 1)):
+            ok, msg = offn.check_close(got, exp)
+            print("current", (b, nc, nv, na, heads), "split", split, name, msg)
+            assert ok, (split, name, msg)
+            if theirs is not None:
+                ok, msg = offn.check_close(got, theirs[i].float())
+                assert ok, (split, name, "reference Triton", msg)
+
+
+def test_masked_block_skip_is_exact(cuda_device):
+    """A mask shared by every head and query row: key blocks with no kept key
+    are skipped, and the result is the same bits as the same mask given per
+    head (no skip)."""
+    from waminfer_b200.attention import masked_attention
+
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    heads, nq, nk = 4, 200, 700
+    q, k, v = _rand(cuda_device, g, 1, nq, heads), _rand(cuda_device, g, 1, nk, heads), _rand(cuda_device, g, 1, nk,
+                                                                                              heads)
+    keep = torch.zeros(nk, dtype=torch.bool, device=cuda_device)
+    keep[:100] = True      # blocks 0 (part); 1, 2 and 4 hold no kept key
+    keep[390:410] = True   # block 3
+    keep[650:] = True      # block 5 (the short last block)
+    shared = keep.view(1, 1, 1, nk)
+    per_head = keep.view(1, 1, 1, nk).expand(1, heads, 1, nk).contiguous()
+    for split in (1, 2, 4):
+        skipped = masked_attention(q, k, v, shared, heads, False, split)
+        dense = masked_attention(q, k, v, per_head, heads, False, split)
+        torch.cuda.synchronize()
+        assert torch.equal(skipped, dense), split
+        ok, msg = offn.check_close(skipped, oattn.masked_attention(q, k, v, shared, heads))
+        assert ok, (split, msg)
+    none_kept = torch.zeros(1, 1, 1, nk, dtype=torch.bool, device=cuda_device)
+    out = masked_attention(q, k, v, none_kept, heads, False, 2)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out) == 0  # every row fully masked: zeros, as SDPA

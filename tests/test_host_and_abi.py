@@ -26,7 +26,7 @@ def test_library_loads_and_exports_every_symbol():
     handle = _lib.lib()
     for name in _lib.EXPORTED_SYMBOLS:
         assert hasattr(handle, name), name
-    assert handle.wamffn_abi_version() == 1
+    assert handle.wamffn_abi_version() == 2
 
 
 def test_abi_rejects_bad_arguments_without_a_gpu():
@@ -180,3 +180,7 @@ def test_attention_abi_rejects_before_launching():
     args.q_batch_stride = 3072 * 391  # rows not at one stride across batches
     assert lib.wamffn_masked_attention(None, ctypes.byref(args)) == 1
     assert b"q strides" in lib.wamffn_last_error()
+    args.q_batch_stride = 3072 * 392
+    args.key_split = 3  # the key split is 1, 2 or 4 CTAs (0: automatic)
+    assert lib.wamffn_masked_attention(None, ctypes.byref(args)) == 1
+    assert b"key_split" in lib.wamffn_last_error()

@@ -52,6 +52,8 @@ EXPORTED_SYMBOLS = (
     "wamffn_block_plan_set_splits",
     "wamffn_block_plan_set_streamk",
     "wamffn_masked_attention",
+    "wamffn_joint_first_frame_attention",
+    "wamffn_current_frame_attention",
     "wamffn_rgb_mandatory",
     "wamffn_select_tokens",
     "wamffn_pack_weight",
@@ -112,6 +114,50 @@ class AttentionArgs(ctypes.Structure):
         ("nk", ctypes.c_int),
         ("heads", ctypes.c_int),
         ("head_dim", ctypes.c_int),
+        ("key_split", ctypes.c_int),
+    ]
+
+
+class RowsView(ctypes.Structure):
+    """Mirror of ``wamffn_rows_view``."""
+
+    _fields_ = [("data", ctypes.c_void_p), ("row_stride", ctypes.c_int64), ("batch_stride", ctypes.c_int64)]
+
+
+class JointAttentionArgs(ctypes.Structure):
+    """Mirror of ``wamffn_joint_attention_args``."""
+
+    _fields_ = [
+        ("q", RowsView),
+        ("k", RowsView),
+        ("v", RowsView),
+        ("out", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("batch", ctypes.c_int),
+        ("count", ctypes.c_int),
+        ("video", ctypes.c_int),
+        ("first", ctypes.c_int),
+        ("heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
+        ("key_split", ctypes.c_int),
+    ]
+
+
+class CurrentFrameArgs(ctypes.Structure):
+    """Mirror of ``wamffn_current_frame_args``."""
+
+    _fields_ = [
+        *[(name, RowsView) for name in ("qv", "qa", "ck", "kv", "ka", "cv", "vv", "va")],
+        ("ov", ctypes.c_void_p),
+        ("oa", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("batch", ctypes.c_int),
+        ("nc", ctypes.c_int),
+        ("nv", ctypes.c_int),
+        ("na", ctypes.c_int),
+        ("heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
+        ("key_split", ctypes.c_int),
     ]
 
 
@@ -230,6 +276,8 @@ def _declare(lib):
     lib.wamffn_block_plan_set_splits.argtypes = [vp, i, i]
     lib.wamffn_block_plan_set_streamk.argtypes = [vp, i]
     lib.wamffn_masked_attention.argtypes = [vp, ctypes.POINTER(AttentionArgs)]
+    lib.wamffn_joint_first_frame_attention.argtypes = [vp, ctypes.POINTER(JointAttentionArgs)]
+    lib.wamffn_current_frame_attention.argtypes = [vp, ctypes.POINTER(CurrentFrameArgs)]
     lib.wamffn_rgb_mandatory.argtypes = [vp, vp, vp, i, i, i, i, vp]
     lib.wamffn_select_tokens.argtypes = [vp, ctypes.POINTER(SelectArgs)]
     lib.wamffn_pack_weight.argtypes = [vp, vp, vp, i, i]
@@ -255,8 +303,8 @@ def lib():
                     )
                 handle = ctypes.CDLL(path)
                 _declare(handle)
-                if handle.wamffn_abi_version() != 1:
-                    raise ImportError(f"{path} has ABI {handle.wamffn_abi_version()}, expected 1")
+                if handle.wamffn_abi_version() != 2:
+                    raise ImportError(f"{path} has ABI {handle.wamffn_abi_version()}, expected 2")
                 _lib = handle
     return _lib
 

@@ -1,22 +1,33 @@
-// Masked multi-head attention of the WAMInfer DiT on tcgen05
-// (the reference's op wam_infer::masked_attention_mask_tiles_v4,
-// WAMInfer/_triton_attention.py:18-145 and :238-263).
+// Multi-head attention of the WAMInfer DiT on tcgen05: the reference's three
+// attention ops (WAMInfer/_triton_attention.py) on one kernel.
 //
-//   out[b, q, h] = softmax_k( q[b, q, h] . k[b, k, h] / sqrt(D) , mask[b, h, q, k] ) . v[b, k, h]
+//   masked_attention_mask_tiles_v4   (:18-145, :238-263)  q against k / v, bool mask [b, h, q, k]
+//   joint_first_frame_attention_v2   (:267-334)           rows [0, first) see keys [0, first), the rest see all
+//   current_frame_attention_v1       (:337-484)           queries (video ++ action) against keys
+//                                                         (context ++ video ++ action), never concatenated
+//
+//   out[b, q, h] = softmax_k( q[b, q, h] . k[b, k, h] / sqrt(D) , masked ) . v[b, k, h]
 //
 // with the reference's arithmetic: scores in fp32, scaled by D^-0.5 log2(e)
-// and exponentiated with exp2; masked keys (and keys past the sequence) at
-// -inf; a running row maximum that is treated as 0 while every key so far is
-// masked (an all-masked row outputs zeros, as SDPA does); probabilities
-// rounded to bf16 before the value product (the reference's
-// probability.to(bf16) dot), the normaliser summed in fp32 from the unrounded
-// probabilities, the fp32 accumulator rescaled by exp2(m_old - m_new) at every
-// key block, scaled by the normaliser's reciprocal at the end, stored as bf16.
+// and exponentiated with exp2; masked keys (and keys past a segment) at -inf;
+// a running row maximum that is treated as 0 while every key so far is masked
+// (an all-masked row outputs zeros, as SDPA does); probabilities rounded to
+// bf16 before the value product (the reference's probability.to(bf16) dot),
+// the normaliser summed in fp32 from the unrounded probabilities, the fp32
+// accumulator rescaled by exp2(m_old - m_new) at every key block, scaled by
+// the normaliser's reciprocal at the end, stored as bf16.
 //
-// One CTA per (128-query tile, head, batch); head dim D = 128.  Key blocks of
-// 128 rows stream through a 2-stage TMA ring (K and V rows as they lie in
-// memory, 128-byte swizzle; K is the K-major operand of Q K^T, V the MN-major
-// operand of P V).  Per key block:
+// Segments.  The queries are up to two row ranges (each with its own tensor
+// map and output rows) and the keys up to three tensors taken as one
+// concatenated sequence; a query segment sees a prefix of that sequence.  Key
+// blocks of 128 rows never straddle two key tensors: a segment's last block is
+// short and its missing keys are masked, which changes only where the blocks
+// start, not the function.
+//
+// One CTA per (128-query tile, head, batch); head dim D = 128.  Key blocks
+// stream through a 2-stage TMA ring (K and V rows as they lie in memory,
+// 128-byte swizzle; K is the K-major operand of Q K^T, V the MN-major operand
+// of P V).  Per key block:
 //   warp 9 (one elected lane): S = Q K^T -> TMEM columns [0, 128)   (M = 128 queries, N = 128 keys)
 //   warps 0-7 (two per TMEM lane quarter: thread = query row x key half):
 //              read S, mask, row maximum (exchanged between the halves), exp2,
@@ -25,6 +36,20 @@
 //   warp 8 (one elected lane): TMA loads of Q once and of K / V per block.
 // Every wait is a clock-bounded spin (the per-block chain is latency-bound);
 // a timed-out wait raises WAMFFN_DEV_TIMEOUT.
+//
+// Masked-block skip: when the mask is shared by every head and query row (a
+// padded text prompt), key blocks in which no key is kept are left out.  Such
+// a block adds exactly nothing (probabilities 0, correction 2^0 = 1), so the
+// skip changes no bit.
+//
+// Key split (grids that would leave SMs idle: the 32-query action rows, the
+// context attention of 2-3 query tiles per head): a cluster of `split` CTAs
+// shares one query tile, each runs the loop above over its share of the key
+// blocks, and the partial (maximum, normaliser, unnormalised O) are combined
+// through distributed shared memory, each CTA producing 128 / split of the
+// output dims.  The split changes where the probabilities' bf16 rounding is
+// taken (against the share's running maximum), as the reference's own choice
+// of key block size does.
 #pragma once
 
 #include "gemm.cuh"
@@ -39,8 +64,11 @@ constexpr int kAttnKeys = 128;      // keys per block (UMMA N of S, K of P.V)
 constexpr int kAttnSoftmaxWarps = 8;  // two warps per TMEM lane quarter: key / dim halves of each row
 constexpr int kAttnThreads = (kAttnSoftmaxWarps + 2) * 32;  // + TMA warp + MMA warp
 constexpr int kAttnTile = kAttnRows * 64 * 2;  // one 128-row x 64-element bf16 operand tile (16 KB)
-// Shared memory: Q (2 tiles), 2 stages of K (2 tiles) + V (2 tiles), P (2 tiles), row exchange.
-constexpr int kAttnSmem = (2 + 2 * 4 + 2) * kAttnTile + 1024 + 256 + 4 * kAttnRows * 4;
+constexpr int kAttnMaxQSeg = 2, kAttnMaxKSeg = 3;
+constexpr int kAttnSkipWords = 64;  // key-block bitmap of the masked-block skip: up to 2048 blocks
+// Shared memory: Q (2 tiles), 2 stages of K (2 tiles) + V (2 tiles), P (2 tiles),
+// barriers, row exchange, skip bitmap.
+constexpr int kAttnSmem = (2 + 2 * 4 + 2) * kAttnTile + 1024 + 256 + 4 * kAttnRows * 4 + kAttnSkipWords * 4;
 
 // V tiles are consumed as an MN-major operand (dims contiguous, the layout
 // TMA writes from V's rows): 64-dim halves 16 KB apart, 8-key groups of the
@@ -48,14 +76,36 @@ constexpr int kAttnSmem = (2 + 2 * 4 + 2) * kAttnTile + 1024 + 256 + 4 * kAttnRo
 constexpr uint32_t kVHalfBytes = kAttnTile;
 constexpr uint32_t kVGroupBytes = 1024;
 
+// The tensor maps of one launch (2-D, [batch x rows, width], box 64 x 128).
+struct AttnMaps {
+  CUtensorMap q[kAttnMaxQSeg];
+  CUtensorMap k[kAttnMaxKSeg];
+  CUtensorMap v[kAttnMaxKSeg];
+};
+
+// A query segment: rows [row0, row0 + rows) of map q[s] in every batch
+// (map row = b * map_batch_rows + row0 + i), written to
+// out + b * out_batch_stride + i * out_row_stride + h * 128.
+struct AttnQSeg {
+  __nv_bfloat16* out;
+  long long out_batch_stride, out_row_stride;  // elements
+  int rows, map_batch_rows, row0;
+  int tiles;    // ceil(rows / 128)
+  int visible;  // keys seen by the segment: a prefix of the concatenated key segments
+};
+
 struct AttnParams {
-  const unsigned char* mask;  // bool, [b, h, q, k] through the strides below, or null
+  const unsigned char* mask;  // bool, [b, h, q, k] through the strides below, or null (one segment each)
   long long mb, mh, mq, mk;   // mask strides in elements (0 = broadcast)
-  __nv_bfloat16* out;         // [batch, nq, heads * D]
-  int heads, nq, nk, batch;
-  float scale_log2;           // D^-0.5 * log2(e)
+  int skip_masked;            // mh == mq == 0: key blocks without a kept key are skipped
+  AttnQSeg qseg[kAttnMaxQSeg];
+  int nqseg;
+  int krows[kAttnMaxKSeg];  // rows per batch of key segment t (map row = b * krows[t] + i)
+  int nkseg;
+  int heads, batch;
+  float scale_log2;  // D^-0.5 * log2(e)
   unsigned int* status;
-  uint32_t v_lbo, v_sbo;      // MN-major descriptor offsets of the V operand (bytes)
+  int split;  // key split: CTAs per cluster sharing one query tile (1, 2 or 4)
 };
 
 // Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled K-major tile.
@@ -72,9 +122,53 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_byte_addr, 
   return d;
 }
 
+// Key blocks of one query segment over the concatenated key segments.
+struct AttnKeyPlan {
+  int blocks[kAttnMaxKSeg];  // 128-key blocks of segment t (of its visible keys)
+  int vis[kAttnMaxKSeg];     // visible keys of segment t
+  int base[kAttnMaxKSeg];    // index of segment t's first key in the concatenation
+  int total;
+};
+
+// One key block: segment, first row in the segment, keys valid from that row,
+// index of the first key in the concatenated sequence.
+struct AttnKeyBlock {
+  int seg, row, valid, key;
+};
+
+__device__ __forceinline__ AttnKeyBlock attn_block(const AttnKeyPlan& kp, int jj) {
+  AttnKeyBlock r;
+  int t = 0;
+  if (jj >= kp.blocks[0]) {
+    jj -= kp.blocks[0];
+    t = 1;
+    if (jj >= kp.blocks[1]) {
+      jj -= kp.blocks[1];
+      t = 2;
+    }
+  }
+  const int vis = t == 0 ? kp.vis[0] : t == 1 ? kp.vis[1] : kp.vis[2];
+  const int base = t == 0 ? kp.base[0] : t == 1 ? kp.base[1] : kp.base[2];
+  r.seg = t;
+  r.row = jj * kAttnKeys;
+  r.valid = min(kAttnKeys, vis - r.row);
+  r.key = base + r.row;
+  return r;
+}
+
+// Index of the n-th (from 0) set bit of the skip bitmap.
+__device__ __forceinline__ int attn_nth_active(const uint32_t* bits, int words, int n) {
+  for (int w = 0; w < words; ++w) {
+    const uint32_t x = bits[w];
+    const int c = __popc(x);
+    if (n < c) return w * 32 + int(__fns(x, 0, n + 1));
+    n -= c;
+  }
+  return 0;  // not reached: n < the bitmap's population
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
-    masked_attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                            const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+    masked_attention_kernel(const __grid_constant__ AttnMaps maps, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = smem;                          // 2 tiles
@@ -89,17 +183,73 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* p_full = bars + 7;
   uint64_t* o_done = bars + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  uint64_t* xch_full = bars + 10;  // key-split combine: the peers' slots have landed
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xmax = reinterpret_cast<float*>(smem + 12 * kAttnTile + 256);  // [2 halves][128 rows]
   float* xsum = xmax + 2 * kAttnRows;                                     // [2 halves][128 rows]
+  uint32_t* skip_bits = reinterpret_cast<uint32_t*>(xsum + 2 * kAttnRows);  // [kAttnSkipWords]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * kAttnRows, h = blockIdx.y, b = blockIdx.z;
-  const int nblocks = (p.nk + kAttnKeys - 1) / kAttnKeys;
+  const int split = p.split;
+  const int ctile = int(blockIdx.x) / split, rank = int(blockIdx.x) - ctile * split;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int seg = (p.nqseg > 1 && ctile >= p.qseg[0].tiles) ? 1 : 0;
+  AttnQSeg qs;  // field by field: no dynamically indexed copy of the parameters
+  qs.out = seg ? p.qseg[1].out : p.qseg[0].out;
+  qs.out_batch_stride = seg ? p.qseg[1].out_batch_stride : p.qseg[0].out_batch_stride;
+  qs.out_row_stride = seg ? p.qseg[1].out_row_stride : p.qseg[0].out_row_stride;
+  qs.rows = seg ? p.qseg[1].rows : p.qseg[0].rows;
+  qs.map_batch_rows = seg ? p.qseg[1].map_batch_rows : p.qseg[0].map_batch_rows;
+  qs.row0 = seg ? p.qseg[1].row0 : p.qseg[0].row0;
+  qs.visible = seg ? p.qseg[1].visible : p.qseg[0].visible;
+  const int q0 = (ctile - (seg ? p.qseg[0].tiles : 0)) * kAttnRows;  // first row of the tile in its segment
+  AttnKeyPlan kp;
+  {
+    int base = 0;
+    kp.total = 0;
+#pragma unroll
+    for (int t = 0; t < kAttnMaxKSeg; ++t) {
+      const int rows = t < p.nkseg ? p.krows[t] : 0;
+      kp.vis[t] = max(0, min(qs.visible - base, rows));
+      kp.blocks[t] = (kp.vis[t] + kAttnKeys - 1) / kAttnKeys;
+      kp.base[t] = base;
+      base += rows;
+      kp.total += kp.blocks[t];
+    }
+  }
   constexpr int kTmaWarp = kAttnSoftmaxWarps, kMmaWarp = kAttnSoftmaxWarps + 1;
+  const int skip_words = (kp.total + 31) / 32;
+
+  // Masked-block skip: which key blocks hold a kept key (one ballot per 32 keys).
+  if (p.skip_masked) {
+    if (threadIdx.x < kAttnSkipWords) skip_bits[threadIdx.x] = 0u;
+    __syncthreads();
+    const int nk = kp.vis[0];  // the skip runs with one key segment
+    for (int k0 = warp * 32; k0 < nk; k0 += kAttnThreads) {
+      const int key = k0 + lane;
+      const bool kept = key < nk && p.mask[size_t(b) * p.mb + size_t(key) * p.mk] != 0;
+      if (__ballot_sync(0xffffffffu, kept) != 0u && lane == 0)
+        atomicOr(&skip_bits[(k0 / kAttnKeys) >> 5], 1u << ((k0 / kAttnKeys) & 31));
+    }
+    __syncthreads();
+  }
+  int active = kp.total;
+  if (p.skip_masked) {
+    active = 0;
+    for (int w = 0; w < skip_words; ++w) active += __popc(skip_bits[w]);
+  }
+  // This CTA's share of the active key blocks: ordinals [jb, jb + nblocks).
+  const int jb = rank * active / split;
+  const int nblocks = (rank + 1) * active / split - jb;
+  auto block_at = [&](int j) {  // the key block of ordinal jb + j
+    const int o = jb + j;
+    return attn_block(kp, p.skip_masked ? attn_nth_active(skip_bits, skip_words, o) : o);
+  };
 
   // Optional phase trace (wamffn_trace_enable): {tag, start, first S ready,
-  // last S ready, last P.V done, end, sm, key blocks}, kind 8.
+  // last S ready (first cluster barrier passed, with a key split), last P.V
+  // done, end, sm | key blocks << 32, the peers' slots landed}, kind 8,
+  // the CTA's rank in its key-split cluster in tag bits 48-51.
   __shared__ unsigned long long* rec;
   if (threadIdx.x == 0) {
     rec = nullptr;
@@ -107,10 +257,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const unsigned int slot = atomicAdd(reinterpret_cast<unsigned int*>(g_trace), 1u);
       if (slot + 1 < g_trace_capacity) {
         rec = g_trace + size_t(slot + 1) * kTraceWords;
-        rec[0] = (unsigned long long)(blockIdx.x | (blockIdx.y << 16)) | (8ull << 32);
+        rec[0] = (unsigned long long)(blockIdx.x | (blockIdx.y << 16)) | (8ull << 32) | ((unsigned long long)rank << 48);
         rec[1] = globaltimer_ns();
-        rec[6] = smid();
-        rec[7] = (unsigned long long)nblocks;
+        rec[6] = smid() | ((unsigned long long)nblocks << 32);
+        rec[7] = 0;
       }
     }
     mbar_init(smem_addr(q_full), 1);
@@ -122,11 +272,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(smem_addr(s_free), kAttnSoftmaxWarps);  // one arrival per softmax warp
     mbar_init(smem_addr(p_full), kAttnSoftmaxWarps);
     mbar_init(smem_addr(o_done), 1);
+    mbar_init(smem_addr(xch_full), 1);
     *abort_flag = 0;
     fence_mbar_init();
-    prefetch_tensormap(&tm_q);
-    prefetch_tensormap(&tm_k);
-    prefetch_tensormap(&tm_v);
+    prefetch_tensormap(&maps.q[seg]);
+    for (int t = 0; t < p.nkseg; ++t) {
+      if (p.krows[t] == 0) continue;  // an empty segment has no map
+      prefetch_tensormap(&maps.k[t]);
+      prefetch_tensormap(&maps.v[t]);
+    }
   }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_addr(tmem_slot), 256);
@@ -140,12 +294,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == kTmaWarp) {
     // ------------------------------------------------------------ TMA loads
-    if (elect_one()) {
+    if (nblocks > 0 && elect_one()) {
       const uint64_t keep = l2_policy_evict_last();  // K / V are re-read by every query tile of the head
       mbar_arrive_expect_tx(smem_addr(q_full), 2 * kAttnTile);
       for (int t = 0; t < 2; ++t)
-        tma_load_2d(smem_addr(q_s + t * kAttnTile), &tm_q, smem_addr(q_full), h * kAttnHeadDim + t * 64,
-                    b * p.nq + q0, keep);
+        tma_load_2d(smem_addr(q_s + t * kAttnTile), &maps.q[seg], smem_addr(q_full), h * kAttnHeadDim + t * 64,
+                    b * qs.map_batch_rows + qs.row0 + q0, keep);
       int issued = 0;
       for (int j = 0; j < nblocks; ++j) {
         const int s = j & 1;
@@ -153,14 +307,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                                     WAMFFN_DEV_TIMEOUT))
           break;
         issued = j + 1;
+        const AttnKeyBlock kb = block_at(j);
+        const int row = b * (kb.seg == 0 ? p.krows[0] : kb.seg == 1 ? p.krows[1] : p.krows[2]) + kb.row;
         uint8_t* st = kv_s + s * 4 * kAttnTile;
         mbar_arrive_expect_tx(smem_addr(&kv_full[s]), 4 * kAttnTile);
         for (int t = 0; t < 2; ++t) {
           // K and V rows of this block, dims [t*64, t*64+64) of the head.
-          tma_load_2d(smem_addr(st + t * kAttnTile), &tm_k, smem_addr(&kv_full[s]), h * kAttnHeadDim + t * 64,
-                      b * p.nk + j * kAttnKeys, keep);
-          tma_load_2d(smem_addr(st + (2 + t) * kAttnTile), &tm_v, smem_addr(&kv_full[s]), h * kAttnHeadDim + t * 64,
-                      b * p.nk + j * kAttnKeys, keep);
+          tma_load_2d(smem_addr(st + t * kAttnTile), &maps.k[kb.seg], smem_addr(&kv_full[s]),
+                      h * kAttnHeadDim + t * 64, row, keep);
+          tma_load_2d(smem_addr(st + (2 + t) * kAttnTile), &maps.v[kb.seg], smem_addr(&kv_full[s]),
+                      h * kAttnHeadDim + t * 64, row, keep);
         }
       }
       if (*abort_flag) {
@@ -171,6 +327,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     __syncwarp();
+    if (split > 1) {  // the softmax warps' two cluster barriers of the key-split combine
+      cluster_sync();
+      cluster_arrive();
+      cluster_wait();
+    }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     const uint32_t idesc_s = umma_idesc_bf16(kAttnRows, kAttnKeys);
@@ -190,11 +351,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       __syncwarp();
     };
-    int ok = 1;
-    if (lane == 0)
-      ok = wait_spin(smem_addr(q_full), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT) &&
-           wait_spin(smem_addr(&kv_full[0]), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
+    int ok = nblocks > 0;
+    if (ok) {
+      if (lane == 0)
+        ok = wait_spin(smem_addr(q_full), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT) &&
+             wait_spin(smem_addr(&kv_full[0]), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
     if (ok) {
       tc_fence_after();
       issue_s(0);
@@ -221,12 +384,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           umma_bf16(tmem_o, umma_desc_sw128(smem_addr(p_s) + (k >> 2) * kAttnTile) + 2 * (k & 3),
-                    umma_desc_sw128_mn(st + 2 * kAttnTile + uint32_t(k) * 2 * kVGroupBytes, p.v_lbo, p.v_sbo),
+                    umma_desc_sw128_mn(st + 2 * kAttnTile + uint32_t(k) * 2 * kVGroupBytes, kVHalfBytes, kVGroupBytes),
                     idesc_o, (j | k) ? 1u : 0u);
         umma_commit(smem_addr(o_done));
         umma_commit(smem_addr(&kv_empty[j & 1]));
       }
       __syncwarp();
+    }
+    if (split > 1) {
+      cluster_sync();
+      cluster_arrive();
+      cluster_wait();
     }
   } else {
     // ------------------------------------------------------ softmax warps
@@ -234,10 +402,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // 128 key columns of S and of the 128 dim columns of O.
     const int r = (warp & 3) * 32 + lane;  // query row within the tile == TMEM lane
     const int half = warp >> 2;
-    const int q = q0 + r;
+    const int q = q0 + r;                  // row within the query segment
     const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
     const unsigned char* mrow =
-        p.mask ? p.mask + size_t(b) * p.mb + size_t(h) * p.mh + size_t(q < p.nq ? q : 0) * p.mq : nullptr;
+        p.mask ? p.mask + size_t(b) * p.mb + size_t(h) * p.mh + size_t(q < qs.rows ? q : 0) * p.mq : nullptr;
     const bool mask_vec = mrow && p.mk == 1 && (reinterpret_cast<uintptr_t>(mrow) & 15u) == 0;
     float m = -INFINITY, l = 0.f;  // l: this half's share of the row's normaliser
     int ok = 1;
@@ -250,7 +418,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       float sc[64];
       float bmax = -INFINITY;
-      const int k0 = j * kAttnKeys + half * 64;
+      const AttnKeyBlock kb = block_at(j);
+      const int k0 = kb.key + half * 64;             // first key of this half in the concatenation
+      const int valid_keys = kb.valid - half * 64;   // keys past the segment are masked
       if (ok) {
         tc_fence_after();
 #pragma unroll
@@ -266,14 +436,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (lane == 0) mbar_arrive_local(smem_addr(s_free));  // S may be overwritten by the next block
         // Scale, mask, this half's maximum.
         if (!mrow) {
-          const int valid_keys = p.nk - k0;  // keys past the sequence are masked
 #pragma unroll
           for (int i = 0; i < 64; ++i) {
             const float v = i < valid_keys ? sc[i] * p.scale_log2 : -INFINITY;
             sc[i] = v;
             bmax = fmaxf(bmax, v);
           }
-        } else if (mask_vec && k0 + 64 <= p.nk) {
+        } else if (mask_vec && valid_keys >= 64) {
 #pragma unroll
           for (int v16 = 0; v16 < 4; ++v16) {
             const uint4 mv = *reinterpret_cast<const uint4*>(mrow + k0 + v16 * 16);
@@ -289,9 +458,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         } else {
 #pragma unroll
           for (int i = 0; i < 64; ++i) {
-            const int key = k0 + i;
-            bool valid = key < p.nk;
-            if (valid && mrow) valid = mrow[size_t(key) * p.mk] != 0;
+            bool valid = i < valid_keys;
+            if (valid) valid = mrow[size_t(k0 + i) * p.mk] != 0;
             const float v = valid ? sc[i] * p.scale_log2 : -INFINITY;
             sc[i] = v;
             bmax = fmaxf(bmax, v);
@@ -304,7 +472,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float other = xmax[(half ^ 1) * kAttnRows + r];
       named_sync(1, kAttnSoftmaxWarps * 32);  // xmax is rewritten by the next block
       if (!ok) continue;
-      if (rec && threadIdx.x == 0) rec[j == 0 ? 2 : 3] = globaltimer_ns();
+      if (rec && threadIdx.x == 0 && (j == 0 || split == 1)) rec[j == 0 ? 2 : 3] = globaltimer_ns();
       const float m_new = fmaxf(m, fmaxf(bmax, other));
       const float safe = m_new == -INFINITY ? 0.f : m_new;
       const float corr = ex2_approx(m - safe);
@@ -351,33 +519,166 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     xsum[half * kAttnRows + r] = l;
     named_sync(1, kAttnSoftmaxWarps * 32);
     const float lt = half == 0 ? l + xsum[kAttnRows + r] : xsum[r] + l;  // fixed order: key half 0 first
-    if (ok) {
+    if (ok && nblocks > 0) {
       if (lane == 0)
         ok = wait_spin(smem_addr(o_done), uint32_t(nblocks - 1) & 1u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
-    if (ok) {
-      if (rec && threadIdx.x == 0) rec[4] = globaltimer_ns();
-      tc_fence_after();
-      const float inv = 1.0f / (lt > 0.f ? lt : 1.0f);  // all-masked rows: O is 0, the output 0
-      __nv_bfloat16* orow = p.out + (size_t(b) * p.nq + q) * size_t(p.heads) * kAttnHeadDim + size_t(h) * kAttnHeadDim +
-                            half * 64;
+    if (ok && rec && threadIdx.x == 0) rec[4] = globaltimer_ns();
+    // O of this CTA (zero when it ran no key block: TMEM then holds nothing).
+    const bool has_o = nblocks > 0;
+    __nv_bfloat16* orow = qs.out + size_t(b) * qs.out_batch_stride + size_t(q < qs.rows ? q : 0) * qs.out_row_stride +
+                          size_t(h) * kAttnHeadDim;
+    if (split == 1) {
+      if (ok) {
+        tc_fence_after();
+        const float inv = 1.0f / (lt > 0.f ? lt : 1.0f);  // all-masked rows: O is 0, the output 0
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem_o + lane_base + uint32_t(half * 64 + c * 32), v);
-        tmem_wait_ld(v);
-        if (q < p.nq) {
+        for (int c = 0; c < 2; ++c) {
+          uint32_t v[32];
+          if (has_o) {
+            tmem_ld32(tmem_o + lane_base + uint32_t(half * 64 + c * 32), v);
+            tmem_wait_ld(v);
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float o[8];
+            for (int i = 0; i < 32; ++i) v[i] = 0u;
+          }
+          if (q < qs.rows) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(v[i + e]) * inv;
-            *reinterpret_cast<uint4*>(orow + c * 32 + i) =
-                make_uint4(bf2_pack(o[0], o[1]), bf2_pack(o[2], o[3]), bf2_pack(o[4], o[5]), bf2_pack(o[6], o[7]));
+            for (int i = 0; i < 32; i += 8) {
+              float o[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o[e] = __uint_as_float(v[i + e]) * inv;
+              *reinterpret_cast<uint4*>(orow + half * 64 + c * 32 + i) = make_uint4(
+                  bf2_pack(o[0], o[1]), bf2_pack(o[2], o[3]), bf2_pack(o[4], o[5]), bf2_pack(o[6], o[7]));
+            }
           }
         }
       }
+    } else {
+      // Key-split combine over the cluster.  CTA c owns output dims
+      // [c W, c W + W), W = 128 / split.  Every CTA stages, for each other
+      // CTA, the 32-dim pieces of its unnormalised O rows that CTA owns and the
+      // rows' (maximum, normaliser), in the receiver's layout, and sends each
+      // staged slot with one bulk copy into the receiver's shared memory.  The
+      // owner rescales the split's partial results to their common maximum and
+      // sums them in rank order:
+      //   O = sum_k O_k 2^(m_k - M),  l = sum_k l_k 2^(m_k - M),  out = O / l.
+      // Receive slots sit in stage 0 of the K / V ring, staged slots in stage
+      // 1; a CTA's ring is free once its last P.V is done, and peers write
+      // into it only after the first cluster barrier.
+      // A slot is [128 rows][2] (m, l), then [128 rows][pitch] O; only the
+      // tile's rows inside the query segment travel.
+      const int W = kAttnHeadDim / split, pitch = W + 4;  // 16-byte row pad: conflict-free 16-byte accesses
+      const int live = min(kAttnRows, qs.rows - q0);      // >= 1
+      const uint32_t slot_bytes = uint32_t(kAttnRows * 8 + kAttnRows * pitch * 4);
+      const uint32_t send_bytes = uint32_t(kAttnRows * 8 + live * pitch * 4);  // a multiple of 16
+      uint8_t* recv = kv_s;                   // [split - 1 senders]
+      uint8_t* stage = kv_s + 4 * kAttnTile;  // [split - 1 receivers]
+      // TMEM loads are warp-wide (.sync.aligned): every lane runs them; only
+      // the shared- and global-memory accesses depend on the row.
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int col = half * 64 + c * 32;
+          const int owner = col / W, off = col - owner * W;
+          if (owner == rank) continue;  // warp-uniform
+          uint32_t v[32];
+          __syncwarp();
+          if (has_o) {
+            tmem_ld32(tmem_o + lane_base + uint32_t(col), v);
+            tmem_wait_ld(v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0u;
+          }
+          if (r < live) {
+            uint8_t* slot = stage + (owner < rank ? owner : owner - 1) * slot_bytes;
+            uint4* dst = reinterpret_cast<uint4*>(slot + kAttnRows * 8 + (r * pitch + off) * 4);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            if (off == 0) *reinterpret_cast<float2*>(slot + r * 8) = make_float2(m, lt);
+          }
+        }
+      }
+      fence_proxy_async();  // the staged slots are read by the bulk copies
+      if (threadIdx.x == 0) mbar_arrive_expect_tx(smem_addr(xch_full), uint32_t(split - 1) * send_bytes);
+      named_sync(1, kAttnSoftmaxWarps * 32);
+      cluster_sync();  // every CTA of the cluster is done with its ring and expects its slots
+      if (rec && threadIdx.x == 0) rec[3] = globaltimer_ns();
+      if (threadIdx.x == 0) {
+        for (int o = 0; o < split; ++o) {
+          if (o == rank) continue;
+          const int slot = rank < o ? rank : rank - 1;  // this CTA's slot in CTA o
+          bulk_copy_to_cta(map_to_cta(smem_addr(recv + slot * slot_bytes), uint32_t(o)),
+                           smem_addr(stage + (o < rank ? o : o - 1) * slot_bytes), send_bytes,
+                           map_to_cta(smem_addr(xch_full), uint32_t(o)));
+        }
+      }
+      int got = 1;
+      if (lane == 0) got = wait_spin(smem_addr(xch_full), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
+      got = __shfl_sync(0xffffffffu, got, 0);
+      cluster_arrive();  // this CTA's incoming slots have landed
+      if (rec && threadIdx.x == 0) rec[7] = globaltimer_ns();
+      if (ok && got) {
+        auto slot_ml = [&](int k) { return reinterpret_cast<const float*>(recv + k * slot_bytes) + r * 2; };
+        const bool row_live = r < live;
+        float top = m;
+        if (row_live)
+          for (int k = 0; k < split - 1; ++k) top = fmaxf(top, slot_ml(k)[0]);
+        const float safe = top == -INFINITY ? 0.f : top;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int col = half * 64 + c * 32;
+          if (col / W != rank) continue;  // warp-uniform
+          const int off = col - rank * W;
+          uint32_t v[32];
+          __syncwarp();
+          if (has_o) {
+            tmem_ld32(tmem_o + lane_base + uint32_t(col), v);
+            tmem_wait_ld(v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0u;
+          }
+          if (!row_live) continue;  // after the warp-wide load; nothing warp-wide follows in this iteration
+          float o[32], lsum = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+          for (int k = 0; k < split; ++k) {  // rank order
+            const int slot = k < rank ? k : k - 1;
+            const float mk = k == rank ? m : slot_ml(slot)[0];
+            const float lk = k == rank ? lt : slot_ml(slot)[1];
+            const float f = ex2_approx(mk - safe);
+            lsum += lk * f;
+            if (k == rank) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] += __uint_as_float(v[i]) * f;
+            } else {
+              const float4* src =
+                  reinterpret_cast<const float4*>(recv + slot * slot_bytes + kAttnRows * 8 + (r * pitch + off) * 4);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 x = src[i];
+                o[4 * i] += x.x * f;
+                o[4 * i + 1] += x.y * f;
+                o[4 * i + 2] += x.z * f;
+                o[4 * i + 3] += x.w * f;
+              }
+            }
+          }
+          const float inv = 1.0f / (lsum > 0.f ? lsum : 1.0f);
+          if (q < qs.rows) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(orow + col + i) =
+                  make_uint4(bf2_pack(o[i] * inv, o[i + 1] * inv), bf2_pack(o[i + 2] * inv, o[i + 3] * inv),
+                             bf2_pack(o[i + 4] * inv, o[i + 5] * inv), bf2_pack(o[i + 6] * inv, o[i + 7] * inv));
+          }
+        }
+      }
+      cluster_wait();  // every slot of the cluster has landed: no copy still reads a CTA's staging
     }
   }
   tc_fence_before();

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -1476,64 +1477,211 @@ int wamffn_rgb_mandatory(void* stream, const void* now, const void* before, int 
   return WAMFFN_OK;
 }
 
-int wamffn_masked_attention(void* stream_, const wamffn_attention_args* a) {
-  if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
-  if (a->head_dim != kAttnHeadDim)
-    return fail(WAMFFN_ERR_UNSUPPORTED, "head_dim=%d: the kernel runs D = %d", a->head_dim, kAttnHeadDim);
-  if (a->batch < 1 || a->nq < 1 || a->nk < 1 || a->heads < 1 || a->batch > 65535 || a->heads > 65535)
-    return fail(WAMFFN_ERR_INVALID, "batch=%d nq=%d nk=%d heads=%d", a->batch, a->nq, a->nk, a->heads);
-  if (!a->q || !a->k || !a->v || !a->out) return fail(WAMFFN_ERR_INVALID, "null tensor pointer");
-  const void* ptrs[] = {a->q, a->k, a->v, a->out};
-  for (const void* p : ptrs)
-    if (!aligned16(p)) return fail(WAMFFN_ERR_INVALID, "tensors must be 16-byte aligned");
-  const int64_t width = int64_t(a->heads) * kAttnHeadDim;
+}  // extern "C"
+
+namespace {
+
+// One [batch, rows, heads*128] operand of the attention ops.
+struct AttnRows {
+  const void* data;
+  int64_t row, batch;  // strides in elements
+  int rows;
+  const char* name;
+};
+
+int check_attn_rows(const AttnRows& v, int64_t width) {
+  if (!v.data) return fail(WAMFFN_ERR_INVALID, "%s is null", v.name);
+  if (!aligned16(v.data)) return fail(WAMFFN_ERR_INVALID, "%s must be 16-byte aligned", v.name);
   // Rows of every batch at one stride (2-D tensor maps over batch x rows).
-  const struct { const char* name; int64_t row, batch; int rows; } views[3] = {
-      {"q", a->q_row_stride, a->q_batch_stride, a->nq},
-      {"k", a->k_row_stride, a->k_batch_stride, a->nk},
-      {"v", a->v_row_stride, a->v_batch_stride, a->nk}};
-  for (const auto& v : views)
-    if (v.row < width || v.row % 8 || v.batch != v.row * v.rows)
-      return fail(WAMFFN_ERR_INVALID,
-                  "%s strides (%lld, %lld): rows must sit at one stride across batches, >= heads*128, a multiple "
-                  "of 8 elements",
-                  v.name, (long long)v.batch, (long long)v.row);
+  if (v.row < width || v.row % 8 || v.batch != v.row * v.rows)
+    return fail(WAMFFN_ERR_INVALID,
+                "%s strides (%lld, %lld): rows must sit at one stride across batches, >= heads*128, a multiple "
+                "of 8 elements",
+                v.name, (long long)v.batch, (long long)v.row);
+  return WAMFFN_OK;
+}
+
+// Tensor map of an operand (no map for an empty one: the kernel never reads it).
+int encode_attn_rows(CUtensorMap* map, const AttnRows& v, int64_t width, int batch) {
+  if (v.rows == 0) return WAMFFN_OK;
+  return encode_operand(map, v.data, uint64_t(width), uint64_t(batch) * v.rows, uint64_t(v.row) * 2, kAttnRows);
+}
+
+int check_attn_shape(int head_dim, int key_split, int batch, int heads) {
+  if (head_dim != kAttnHeadDim)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "head_dim=%d: the kernel runs D = %d", head_dim, kAttnHeadDim);
+  if (key_split != 0 && key_split != 1 && key_split != 2 && key_split != 4)
+    return fail(WAMFFN_ERR_INVALID, "key_split=%d: 0 (automatic), 1, 2 or 4", key_split);
+  if (batch < 1 || heads < 1 || batch > 65535 || heads > 65535)
+    return fail(WAMFFN_ERR_INVALID, "batch=%d heads=%d", batch, heads);
+  return WAMFFN_OK;
+}
+
+// Grid, key split and launch of masked_attention_kernel for segments already
+// described in `p` (tiles filled in here).
+int launch_attention(void* stream_, const AttnMaps& maps, AttnParams& p, int key_split) {
   int dev = 0, sm = 0;
   WAMFFN_CUDA(cudaGetDevice(&dev));
   int rc = prepare_device(dev, &sm);
   if (rc) return rc;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  CUtensorMap tm_q, tm_k, tm_v;
-  rc = encode_operand(&tm_q, a->q, uint64_t(width), uint64_t(a->batch) * a->nq, uint64_t(a->q_row_stride) * 2,
-                      kAttnRows);
+  int64_t tiles = 0;
+  int max_blocks = 0;
+  for (int s = 0; s < p.nqseg; ++s) {
+    p.qseg[s].tiles = (p.qseg[s].rows + kAttnRows - 1) / kAttnRows;
+    tiles += p.qseg[s].tiles;
+    int blocks = 0, base = 0;
+    for (int t = 0; t < p.nkseg; ++t) {
+      const int vis = std::max(0, std::min(p.qseg[s].visible - base, p.krows[t]));
+      blocks += (vis + kAttnKeys - 1) / kAttnKeys;
+      base += p.krows[t];
+    }
+    if (p.qseg[s].rows > 0) max_blocks = std::max(max_blocks, blocks);
+  }
+  if (tiles == 0) return WAMFFN_OK;
+  // Key split: the largest of 1, 2, 4 that keeps the grid within one wave
+  // (one CTA per SM), or the caller's; halved while it exceeds the key blocks
+  // of the longest query tile.
+  const int64_t ctas = tiles * p.heads * p.batch;
+  int split = 1;
+  if (key_split) {
+    split = key_split;
+  } else {
+    for (int s : {2, 4})
+      if (ctas * s <= sm) split = s;
+  }
+  while (split > 1 && split > max_blocks) split >>= 1;
+  if (tiles * split > 0x7fffffff) return fail(WAMFFN_ERR_INVALID, "too many query rows");
+  p.split = split;
+  p.scale_log2 = float((1.0 / sqrt(double(kAttnHeadDim))) * 1.4426950408889634);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(unsigned(tiles * split), unsigned(p.heads), unsigned(p.batch));
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = kAttnSmem;
+  cfg.stream = static_cast<cudaStream_t>(stream_);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(split);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel, maps, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return WAMFFN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wamffn_masked_attention(void* stream_, const wamffn_attention_args* a) {
+  if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
+  int rc = check_attn_shape(a->head_dim, a->key_split, a->batch, a->heads);
   if (rc) return rc;
-  rc = encode_operand(&tm_k, a->k, uint64_t(width), uint64_t(a->batch) * a->nk, uint64_t(a->k_row_stride) * 2,
-                      kAttnKeys);
-  if (rc) return rc;
-  rc = encode_operand(&tm_v, a->v, uint64_t(width), uint64_t(a->batch) * a->nk, uint64_t(a->v_row_stride) * 2,
-                      kAttnKeys);
-  if (rc) return rc;
+  if (a->nq < 1 || a->nk < 1) return fail(WAMFFN_ERR_INVALID, "nq=%d nk=%d", a->nq, a->nk);
+  if (!a->out || !aligned16(a->out)) return fail(WAMFFN_ERR_INVALID, "out must be a 16-byte aligned pointer");
+  const int64_t width = int64_t(a->heads) * kAttnHeadDim;
+  const AttnRows views[3] = {{a->q, a->q_row_stride, a->q_batch_stride, a->nq, "q"},
+                             {a->k, a->k_row_stride, a->k_batch_stride, a->nk, "k"},
+                             {a->v, a->v_row_stride, a->v_batch_stride, a->nk, "v"}};
+  for (const auto& v : views)
+    if ((rc = check_attn_rows(v, width))) return rc;
+  AttnMaps maps{};
+  if ((rc = encode_attn_rows(&maps.q[0], views[0], width, a->batch))) return rc;
+  if ((rc = encode_attn_rows(&maps.k[0], views[1], width, a->batch))) return rc;
+  if ((rc = encode_attn_rows(&maps.v[0], views[2], width, a->batch))) return rc;
   AttnParams p{};
   p.mask = static_cast<const unsigned char*>(a->mask);
   p.mb = a->mask_strides[0];
   p.mh = a->mask_strides[1];
   p.mq = a->mask_strides[2];
   p.mk = a->mask_strides[3];
-  p.out = static_cast<__nv_bfloat16*>(a->out);
+  // A mask shared by every head and query row lets fully masked key blocks be skipped.
+  p.skip_masked = a->mask && p.mh == 0 && p.mq == 0 &&
+                  (a->nk + kAttnKeys - 1) / kAttnKeys <= kAttnSkipWords * 32;
+  p.qseg[0] = AttnQSeg{static_cast<__nv_bfloat16*>(a->out), int64_t(a->nq) * width, width, a->nq, a->nq, 0, 0, a->nk};
+  p.nqseg = 1;
+  p.krows[0] = a->nk;
+  p.nkseg = 1;
   p.heads = a->heads;
-  p.nq = a->nq;
-  p.nk = a->nk;
   p.batch = a->batch;
-  p.scale_log2 = float((1.0 / sqrt(double(kAttnHeadDim))) * 1.4426950408889634);
   p.status = static_cast<unsigned int*>(a->status);
-  static const int vdesc = env_int("WAMFFN_ATTN_VDESC", 0);
-  p.v_lbo = vdesc ? kVGroupBytes : kVHalfBytes;
-  p.v_sbo = vdesc ? kVHalfBytes : kVGroupBytes;
-  dim3 grid(unsigned((a->nq + kAttnRows - 1) / kAttnRows), unsigned(a->heads), unsigned(a->batch));
-  masked_attention_kernel<<<grid, kAttnThreads, kAttnSmem, stream>>>(tm_q, tm_k, tm_v, p);
-  WAMFFN_CUDA(cudaGetLastError());
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  return WAMFFN_OK;
+  return launch_attention(stream_, maps, p, a->key_split);
+}
+
+int wamffn_joint_first_frame_attention(void* stream_, const wamffn_joint_attention_args* a) {
+  if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
+  int rc = check_attn_shape(a->head_dim, a->key_split, a->batch, a->heads);
+  if (rc) return rc;
+  if (a->count < 1 || a->first < 0 || a->first > a->count)
+    return fail(WAMFFN_ERR_INVALID, "count=%d first=%d: 0 <= first <= count, count >= 1", a->count, a->first);
+  if (!a->out || !aligned16(a->out)) return fail(WAMFFN_ERR_INVALID, "out must be a 16-byte aligned pointer");
+  const int64_t width = int64_t(a->heads) * kAttnHeadDim;
+  const AttnRows views[3] = {{a->q.data, a->q.row_stride, a->q.batch_stride, a->count, "q"},
+                             {a->k.data, a->k.row_stride, a->k.batch_stride, a->count, "k"},
+                             {a->v.data, a->v.row_stride, a->v.batch_stride, a->count, "v"}};
+  for (const auto& v : views)
+    if ((rc = check_attn_rows(v, width))) return rc;
+  AttnMaps maps{};
+  if ((rc = encode_attn_rows(&maps.q[0], views[0], width, a->batch))) return rc;
+  maps.q[1] = maps.q[0];
+  if ((rc = encode_attn_rows(&maps.k[0], views[1], width, a->batch))) return rc;
+  if ((rc = encode_attn_rows(&maps.v[0], views[2], width, a->batch))) return rc;
+  AttnParams p{};
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a->out);
+  // Clean first-frame rows see the first frame's keys; every other row sees all.
+  p.qseg[0] = AttnQSeg{out, int64_t(a->count) * width, width, a->first, a->count, 0, 0, a->first};
+  p.qseg[1] = AttnQSeg{out + int64_t(a->first) * width, int64_t(a->count) * width, width, a->count - a->first,
+                       a->count, a->first, 0, a->count};
+  p.nqseg = 2;
+  p.krows[0] = a->count;
+  p.nkseg = 1;
+  p.heads = a->heads;
+  p.batch = a->batch;
+  p.status = static_cast<unsigned int*>(a->status);
+  return launch_attention(stream_, maps, p, a->key_split);
+}
+
+int wamffn_current_frame_attention(void* stream_, const wamffn_current_frame_args* a) {
+  if (!a) return fail(WAMFFN_ERR_INVALID, "args is null");
+  int rc = check_attn_shape(a->head_dim, a->key_split, a->batch, a->heads);
+  if (rc) return rc;
+  if (a->nc < 0 || a->nv < 0 || a->na < 0 || a->nv + a->na < 1 || int64_t(a->nc) + a->nv + a->na > 0x7fffffff)
+    return fail(WAMFFN_ERR_INVALID, "nc=%d nv=%d na=%d", a->nc, a->nv, a->na);
+  const int64_t width = int64_t(a->heads) * kAttnHeadDim;
+  const AttnRows qv{a->qv.data, a->qv.row_stride, a->qv.batch_stride, a->nv, "qv"};
+  const AttnRows qa{a->qa.data, a->qa.row_stride, a->qa.batch_stride, a->na, "qa"};
+  const AttnRows keys[3] = {{a->ck.data, a->ck.row_stride, a->ck.batch_stride, a->nc, "ck"},
+                            {a->kv.data, a->kv.row_stride, a->kv.batch_stride, a->nv, "kv"},
+                            {a->ka.data, a->ka.row_stride, a->ka.batch_stride, a->na, "ka"}};
+  const AttnRows values[3] = {{a->cv.data, a->cv.row_stride, a->cv.batch_stride, a->nc, "cv"},
+                              {a->vv.data, a->vv.row_stride, a->vv.batch_stride, a->nv, "vv"},
+                              {a->va.data, a->va.row_stride, a->va.batch_stride, a->na, "va"}};
+  const AttnRows all[8] = {qv, qa, keys[0], keys[1], keys[2], values[0], values[1], values[2]};
+  for (const auto& v : all)
+    if (v.rows > 0 && (rc = check_attn_rows(v, width))) return rc;
+  if ((a->nv > 0 && (!a->ov || !aligned16(a->ov))) || (a->na > 0 && (!a->oa || !aligned16(a->oa))))
+    return fail(WAMFFN_ERR_INVALID, "ov / oa must be 16-byte aligned pointers");
+  AttnMaps maps{};
+  if ((rc = encode_attn_rows(&maps.q[0], qv, width, a->batch))) return rc;
+  if ((rc = encode_attn_rows(&maps.q[1], qa, width, a->batch))) return rc;
+  for (int t = 0; t < 3; ++t) {
+    if ((rc = encode_attn_rows(&maps.k[t], keys[t], width, a->batch))) return rc;
+    if ((rc = encode_attn_rows(&maps.v[t], values[t], width, a->batch))) return rc;
+  }
+  AttnParams p{};
+  const int total = a->nc + a->nv + a->na;
+  p.qseg[0] = AttnQSeg{static_cast<__nv_bfloat16*>(a->ov), int64_t(a->nv) * width, width, a->nv, a->nv, 0, 0, total};
+  p.qseg[1] = AttnQSeg{static_cast<__nv_bfloat16*>(a->oa), int64_t(a->na) * width, width, a->na, a->na, 0, 0, total};
+  p.nqseg = 2;
+  p.krows[0] = a->nc;
+  p.krows[1] = a->nv;
+  p.krows[2] = a->na;
+  p.nkseg = 3;
+  p.heads = a->heads;
+  p.batch = a->batch;
+  p.status = static_cast<unsigned int*>(a->status);
+  return launch_attention(stream_, maps, p, a->key_split);
 }
 
 }  // extern "C"

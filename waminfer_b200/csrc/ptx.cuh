@@ -243,6 +243,22 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The two halves of cluster_sync, for work between arriving and waiting.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory to another CTA's (shared::cluster address), whose
+// mbarrier `bar` (shared::cluster address) receives the bytes as complete_tx.
+__device__ __forceinline__ void bulk_copy_to_cta(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 template <int kGroup>
 __device__ __forceinline__ void tmem_alloc_g(uint32_t dst_smem, uint32_t ncols) {

@@ -22,8 +22,10 @@ import torch
 from waminfer_b200 import _lib
 
 WORDS = 8
-KINDS = {0: "gemm: bias + GELU", 1: "gemm: bias", 2: "gemm: split-K partials", 7: "layer boundary"}
+KINDS = {0: "gemm: bias + GELU", 1: "gemm: bias", 2: "gemm: split-K partials", 7: "layer boundary",
+         8: "masked attention"}
 BOUNDARY = 7
+ATTENTION = 8
 
 
 def decode(buffer: torch.Tensor) -> list[dict]:
@@ -37,6 +39,11 @@ def decode(buffer: torch.Tensor) -> list[dict]:
         rec = {"kind": kind, "x": tag & 0xFFFF, "y": (tag >> 16) & 0xFFFF, "sm": w[6], "start": w[1], "end": w[5]}
         if kind == BOUNDARY:
             rec.update(waited=w[2], reduced=w[3])
+        elif kind == ATTENTION:
+            # {first S ready, last S ready or first cluster barrier, last P.V done,
+            #  sm | key blocks << 32, second cluster barrier}; rank in tag bits 48-51
+            rec.update(sm=w[6] & 0xFFFFFFFF, key_blocks=w[6] >> 32, rank=(tag >> 48) & 0xF, first_s=w[2],
+                       last_s_or_combine=w[3], last_pv=w[4], exchanged=w[7])
         else:
             rec.update(ready=w[2], issued=w[3], epilogue=w[4], k_blocks=w[7])
         out.append(rec)
@@ -73,6 +80,9 @@ def group_launches(records: list[dict]) -> list[dict]:
         if kind == BOUNDARY:
             summary.update(wait_us=span("start", "waited"), reduce_us=span("waited", "reduced"),
                            finish_us=span("reduced", "end"))
+        elif kind == ATTENTION:
+            summary.update(setup_us=span("start", "first_s"), mainloop_us=span("first_s", "last_pv"),
+                           epilogue_us=span("last_pv", "end"))
         else:
             summary.update(setup_us=span("start", "ready"), mainloop_us=span("ready", "issued"),
                            epilogue_us=span("epilogue", "end"))
