@@ -3,7 +3,10 @@
  * PreparedFFN.forward through wamffn_pack_weight + wamffn_linear_plan_create
  * + wamffn_ffn_run on a small seeded case, checked against a CPU restatement
  * (fp32 sums, bias and tanh-GELU in fp32, bf16 rounding of the hidden and the
- * output, as the prepared path does).  Built and run by tests/test_gpu_c_abi.py.
+ * output, as the prepared path does); then wamffn_masked_attention with a
+ * padded-prompt key mask, checked against a CPU softmax with the
+ * probabilities rounded to bf16 before the value product.  Built and run by
+ * tests/test_gpu_c_abi.py.
  *
  * Exit status 0 when every output is within max(2e-2, one bf16 ulp) of the
  * restatement and mean |error| / mean |reference| is below 5e-3 (the rule of
@@ -19,6 +22,7 @@
 #include "wamffn.h"
 
 enum { ROWS = 40, D = 256, H = 512 };
+enum { HEADS = 2, NQ = 40, NK = 70, KEPT = 60, W = HEADS * 128 };
 
 static uint16_t to_bf16(float f) {
   uint32_t u;
@@ -138,7 +142,64 @@ int main(void) {
   const double rel = err_sum / (ref_sum > 1e-12 ? ref_sum : 1e-12);
   wamffn_linear_plan_destroy(up);
   wamffn_linear_plan_destroy(down);
-  cudaStreamDestroy(stream);
   printf("c abi ffn: %d of %d outside tolerance, mean relative error %.2e\n", bad_count, ROWS * D, rel);
-  return (bad_count == 0 && rel < 5e-3) ? 0 : 1;
+
+  /* Masked attention: keys [KEPT, NK) masked for every head and query (a padded prompt). */
+  static uint16_t q[NQ * W], k[NK * W], v[NK * W], o[NQ * W];
+  static unsigned char mask[NK];
+  for (int i = 0; i < NQ * W; ++i) q[i] = to_bf16(gauss());
+  for (int i = 0; i < NK * W; ++i) k[i] = to_bf16(gauss());
+  for (int i = 0; i < NK * W; ++i) v[i] = to_bf16(gauss());
+  for (int i = 0; i < NK; ++i) mask[i] = i < KEPT;
+  void *dq, *dk, *dv, *dmask, *dobuf;
+  CHECK_CUDA(cudaMalloc(&dq, sizeof q));
+  CHECK_CUDA(cudaMalloc(&dk, sizeof k));
+  CHECK_CUDA(cudaMalloc(&dv, sizeof v));
+  CHECK_CUDA(cudaMalloc(&dmask, sizeof mask));
+  CHECK_CUDA(cudaMalloc(&dobuf, sizeof o));
+  CHECK_CUDA(cudaMemcpy(dq, q, sizeof q, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(dk, k, sizeof k, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(dv, v, sizeof v, cudaMemcpyHostToDevice));
+  CHECK_CUDA(cudaMemcpy(dmask, mask, sizeof mask, cudaMemcpyHostToDevice));
+  wamffn_attention_args at;
+  memset(&at, 0, sizeof at);
+  at.q = dq; at.q_row_stride = W; at.q_batch_stride = (int64_t)W * NQ;
+  at.k = dk; at.k_row_stride = W; at.k_batch_stride = (int64_t)W * NK;
+  at.v = dv; at.v_row_stride = W; at.v_batch_stride = (int64_t)W * NK;
+  at.mask = dmask; at.mask_strides[3] = 1; /* [1, 1, 1, NK] broadcast over heads and queries */
+  at.out = dobuf; at.batch = 1; at.nq = NQ; at.nk = NK; at.heads = HEADS; at.head_dim = 128;
+  CHECK_ABI(wamffn_masked_attention(stream, &at));
+  CHECK_CUDA(cudaStreamSynchronize(stream));
+  CHECK_CUDA(cudaMemcpy(o, dobuf, sizeof o, cudaMemcpyDeviceToHost));
+  int attn_bad = 0;
+  double aerr = 0.0, aref = 0.0;
+  for (int h = 0; h < HEADS; ++h) {
+    for (int i = 0; i < NQ; ++i) {
+      float s[NK], top = -INFINITY, norm = 0.0f;
+      for (int j = 0; j < KEPT; ++j) {
+        float acc = 0.0f;
+        for (int d = 0; d < 128; ++d) acc += from_bf16(q[i * W + h * 128 + d]) * from_bf16(k[j * W + h * 128 + d]);
+        s[j] = acc * 0.08838834764831845f * 1.4426950408889634f;
+        top = fmaxf(top, s[j]);
+      }
+      for (int j = 0; j < KEPT; ++j) {
+        s[j] = exp2f(s[j] - top);
+        norm += s[j];
+      }
+      for (int d = 0; d < 128; ++d) {
+        float acc = 0.0f;
+        for (int j = 0; j < KEPT; ++j) acc += round_bf16(s[j]) * from_bf16(v[j * W + h * 128 + d]);
+        const float ref = acc / norm;
+        const float got = from_bf16(o[i * W + h * 128 + d]);
+        const float ulp = ldexpf(1.0f, (int)floorf(log2f(fabsf(ref) + 1e-30f)) - 7);
+        if (fabsf(got - ref) > fmaxf(2e-2f, ulp)) ++attn_bad;
+        aerr += fabsf(got - ref);
+        aref += fabsf(ref);
+      }
+    }
+  }
+  const double arel = aerr / (aref > 1e-12 ? aref : 1e-12);
+  cudaStreamDestroy(stream);
+  printf("c abi attention: %d of %d outside tolerance, mean relative error %.2e\n", attn_bad, NQ * W, arel);
+  return (bad_count == 0 && rel < 5e-3 && attn_bad == 0 && arel < 5e-3) ? 0 : 1;
 }

@@ -1,7 +1,8 @@
 """GPU: the C ABI from a plain C program (tests/c_abi_ffn.c), compiled with
 gcc against include/wamffn.h and the in-tree libwamffn.so and the CUDA
 runtime: pack, plan (tuned), FFN run and status, checked in C against a CPU
-restatement of the prepared FFN, and an invalid plan rejected with a message."""
+restatement of the prepared FFN, an invalid plan rejected with a message, and
+the masked attention with a padded-prompt mask against a CPU softmax."""
 
 import os
 import shutil
@@ -31,4 +32,4 @@ def test_c_program_runs_the_ffn_through_the_abi(cuda_device, tmp_path):
                    check=True, capture_output=True, text=True, timeout=120)
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert run.returncode == 0, run.stdout + run.stderr
-    assert "0 of" in run.stdout
+    assert "ffn: 0 of" in run.stdout and "attention: 0 of" in run.stdout

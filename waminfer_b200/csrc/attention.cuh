@@ -176,14 +176,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* p_s = smem + 10 * kAttnTile;         // 2 tiles
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 12 * kAttnTile);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
-  uint64_t* xch_full = bars + 10;  // key-split combine: the peers' slots have landed
+  uint64_t* k_full = bars + 1;    // [2]  K of a stage landed (S needs only K)
+  uint64_t* v_full = bars + 3;    // [2]  V of a stage landed
+  uint64_t* kv_empty = bars + 5;  // [2]
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_free = bars + 8;
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint64_t* xch_full = bars + 11;  // key-split combine: the peers' slots have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xmax = reinterpret_cast<float*>(smem + 12 * kAttnTile + 256);  // [2 halves][128 rows]
   float* xsum = xmax + 2 * kAttnRows;                                     // [2 halves][128 rows]
@@ -220,6 +221,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr int kTmaWarp = kAttnSoftmaxWarps, kMmaWarp = kAttnSoftmaxWarps + 1;
   const int skip_words = (kp.total + 31) / 32;
 
+  const bool tma_lane = threadIdx.x == kTmaWarp * 32;  // sets up the barriers and issues every TMA load
+  if (tma_lane) {
+    mbar_init(smem_addr(q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_addr(&k_full[s]), 1);
+      mbar_init(smem_addr(&v_full[s]), 1);
+      mbar_init(smem_addr(&kv_empty[s]), 1);
+    }
+    mbar_init(smem_addr(s_full), 1);
+    mbar_init(smem_addr(s_free), kAttnSoftmaxWarps);  // one arrival per softmax warp
+    mbar_init(smem_addr(p_full), kAttnSoftmaxWarps);
+    mbar_init(smem_addr(o_done), 1);
+    mbar_init(smem_addr(xch_full), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&maps.q[seg]);
+    for (int t = 0; t < p.nkseg; ++t) {
+      if (p.krows[t] == 0) continue;  // an empty segment has no map
+      prefetch_tensormap(&maps.k[t]);
+      prefetch_tensormap(&maps.v[t]);
+    }
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(smem_addr(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel on the stream; global memory is touched only after it completed.
+  pdl_wait_prior();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
   // Masked-block skip: which key blocks hold a kept key (one ballot per 32 keys).
   if (p.skip_masked) {
     if (threadIdx.x < kAttnSkipWords) skip_bits[threadIdx.x] = 0u;
@@ -246,6 +278,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     return attn_block(kp, p.skip_masked ? attn_nth_active(skip_bits, skip_words, o) : o);
   };
 
+  // TMA loads (issued by tma_lane only): Q once, K and V of block j into ring stage j & 1.
+  const uint64_t keep = l2_policy_evict_last();  // K / V are re-read by every query tile of the head
+  auto issue_q = [&]() {
+    mbar_arrive_expect_tx(smem_addr(q_full), 2 * kAttnTile);
+    for (int t = 0; t < 2; ++t)
+      tma_load_2d(smem_addr(q_s + t * kAttnTile), &maps.q[seg], smem_addr(q_full), h * kAttnHeadDim + t * 64,
+                  b * qs.map_batch_rows + qs.row0 + q0, keep);
+  };
+  auto issue_kv = [&](int j) {
+    const int s = j & 1;
+    const AttnKeyBlock kb = block_at(j);
+    const int row = b * (kb.seg == 0 ? p.krows[0] : kb.seg == 1 ? p.krows[1] : p.krows[2]) + kb.row;
+    uint8_t* st = kv_s + s * 4 * kAttnTile;
+    // K and V rows of this block, dims [t*64, t*64+64) of the head, on separate barriers.
+    mbar_arrive_expect_tx(smem_addr(&k_full[s]), 2 * kAttnTile);
+    for (int t = 0; t < 2; ++t)
+      tma_load_2d(smem_addr(st + t * kAttnTile), &maps.k[kb.seg], smem_addr(&k_full[s]), h * kAttnHeadDim + t * 64,
+                  row, keep);
+    mbar_arrive_expect_tx(smem_addr(&v_full[s]), 2 * kAttnTile);
+    for (int t = 0; t < 2; ++t)
+      tma_load_2d(smem_addr(st + (2 + t) * kAttnTile), &maps.v[kb.seg], smem_addr(&v_full[s]),
+                  h * kAttnHeadDim + t * 64, row, keep);
+  };
+  // Without the skip the key blocks are known now: Q and the first two blocks
+  // go out before the block-wide barrier.
+  const int early = (!p.skip_masked && nblocks > 0) ? min(nblocks, 2) : 0;
+  if (tma_lane && early) {
+    issue_q();
+    for (int j = 0; j < early; ++j) issue_kv(j);
+  }
+
   // Optional phase trace (wamffn_trace_enable): {tag, start, first S ready,
   // last S ready (first cluster barrier passed, with a key split), last P.V
   // done, end, sm | key blocks << 32, the peers' slots landed}, kind 8,
@@ -263,28 +326,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         rec[7] = 0;
       }
     }
-    mbar_init(smem_addr(q_full), 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_addr(&kv_full[s]), 1);
-      mbar_init(smem_addr(&kv_empty[s]), 1);
-    }
-    mbar_init(smem_addr(s_full), 1);
-    mbar_init(smem_addr(s_free), kAttnSoftmaxWarps);  // one arrival per softmax warp
-    mbar_init(smem_addr(p_full), kAttnSoftmaxWarps);
-    mbar_init(smem_addr(o_done), 1);
-    mbar_init(smem_addr(xch_full), 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    prefetch_tensormap(&maps.q[seg]);
-    for (int t = 0; t < p.nkseg; ++t) {
-      if (p.krows[t] == 0) continue;  // an empty segment has no map
-      prefetch_tensormap(&maps.k[t]);
-      prefetch_tensormap(&maps.v[t]);
-    }
-  }
-  if (warp == kMmaWarp) {
-    tmem_alloc(smem_addr(tmem_slot), 256);
-    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
@@ -294,36 +335,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == kTmaWarp) {
     // ------------------------------------------------------------ TMA loads
-    if (nblocks > 0 && elect_one()) {
-      const uint64_t keep = l2_policy_evict_last();  // K / V are re-read by every query tile of the head
-      mbar_arrive_expect_tx(smem_addr(q_full), 2 * kAttnTile);
-      for (int t = 0; t < 2; ++t)
-        tma_load_2d(smem_addr(q_s + t * kAttnTile), &maps.q[seg], smem_addr(q_full), h * kAttnHeadDim + t * 64,
-                    b * qs.map_batch_rows + qs.row0 + q0, keep);
-      int issued = 0;
-      for (int j = 0; j < nblocks; ++j) {
-        const int s = j & 1;
-        if (j >= 2 && !wait_spin(smem_addr(&kv_empty[s]), uint32_t((j >> 1) - 1) & 1u, abort_flag, p.status,
+    if (nblocks > 0 && lane == 0) {
+      if (!early) issue_q();
+      int issued = early;
+      for (int j = early; j < nblocks; ++j) {
+        if (j >= 2 && !wait_spin(smem_addr(&kv_empty[j & 1]), uint32_t((j >> 1) - 1) & 1u, abort_flag, p.status,
                                     WAMFFN_DEV_TIMEOUT))
           break;
+        issue_kv(j);
         issued = j + 1;
-        const AttnKeyBlock kb = block_at(j);
-        const int row = b * (kb.seg == 0 ? p.krows[0] : kb.seg == 1 ? p.krows[1] : p.krows[2]) + kb.row;
-        uint8_t* st = kv_s + s * 4 * kAttnTile;
-        mbar_arrive_expect_tx(smem_addr(&kv_full[s]), 4 * kAttnTile);
-        for (int t = 0; t < 2; ++t) {
-          // K and V rows of this block, dims [t*64, t*64+64) of the head.
-          tma_load_2d(smem_addr(st + t * kAttnTile), &maps.k[kb.seg], smem_addr(&kv_full[s]),
-                      h * kAttnHeadDim + t * 64, row, keep);
-          tma_load_2d(smem_addr(st + (2 + t) * kAttnTile), &maps.v[kb.seg], smem_addr(&kv_full[s]),
-                      h * kAttnHeadDim + t * 64, row, keep);
-        }
       }
       if (*abort_flag) {
         // Let the copies still in flight land before the CTA gives up its shared memory.
         wait_drain(smem_addr(q_full), 0u);
-        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j)
-          wait_drain(smem_addr(&kv_full[j & 1]), uint32_t(j >> 1) & 1u);
+        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
+          wait_drain(smem_addr(&k_full[j & 1]), uint32_t(j >> 1) & 1u);
+          wait_drain(smem_addr(&v_full[j & 1]), uint32_t(j >> 1) & 1u);
+        }
       }
     }
     __syncwarp();
@@ -336,8 +364,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------ MMA issue
     const uint32_t idesc_s = umma_idesc_bf16(kAttnRows, kAttnKeys);
     const uint32_t idesc_o = umma_idesc_bf16(kAttnRows, kAttnHeadDim) | (1u << 16);  // B (V) MN-major
-    // S of block j + 1 is issued as soon as the softmax has read S of block j,
-    // ahead of block j's P.V, so that it is computed while the softmax works.
+    // S of block j + 1 is issued as soon as the softmax has read S of block j
+    // and K of block j + 1 has landed, ahead of block j's P.V, so that it is
+    // computed while the softmax works.
     auto issue_s = [&](int j) {
       const uint32_t st = smem_addr(kv_s + (j & 1) * 4 * kAttnTile);
       if (elect_one()) {
@@ -355,7 +384,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (ok) {
       if (lane == 0)
         ok = wait_spin(smem_addr(q_full), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT) &&
-             wait_spin(smem_addr(&kv_full[0]), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
+             wait_spin(smem_addr(&k_full[0]), 0u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (ok) {
@@ -365,7 +394,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int j = 0; j < nblocks && ok; ++j) {
       if (j + 1 < nblocks) {
         if (lane == 0)
-          ok = wait_spin(smem_addr(&kv_full[(j + 1) & 1]), uint32_t((j + 1) >> 1) & 1u, abort_flag, p.status,
+          ok = wait_spin(smem_addr(&k_full[(j + 1) & 1]), uint32_t((j + 1) >> 1) & 1u, abort_flag, p.status,
                          WAMFFN_DEV_TIMEOUT) &&
                wait_spin(smem_addr(s_free), uint32_t(j) & 1u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -373,7 +402,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         issue_s(j + 1);
       }
-      if (lane == 0) ok = wait_spin(smem_addr(p_full), uint32_t(j) & 1u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
+      if (lane == 0)
+        ok = wait_spin(smem_addr(&v_full[j & 1]), uint32_t(j >> 1) & 1u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT) &&
+             wait_spin(smem_addr(p_full), uint32_t(j) & 1u, abort_flag, p.status, WAMFFN_DEV_TIMEOUT);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();

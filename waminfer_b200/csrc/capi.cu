@@ -1558,13 +1558,17 @@ int launch_attention(void* stream_, const AttnMaps& maps, AttnParams& p, int key
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = kAttnSmem;
   cfg.stream = static_cast<cudaStream_t>(stream_);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = unsigned(split);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // Programmatic dependent launch: barrier set-up and TMEM allocation overlap
+  // the previous kernel; the kernel waits for it before touching global memory.
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel, maps, p));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;
