@@ -15,14 +15,15 @@ synthetic values; everything runs in bf16 on the GPU with the reference's
 Triton kernels (Q/K RMSNorm + RoPE, modulated norms, masked attention).
 
 The reference package is imported from baseline/_ref through the stub parent
-package of baseline/reference_phase.py.
+package of baseline/reference_phase.py; ``reference_graphs`` adds the
+reference's CUDA-graph wrapper.
 """
 
 from __future__ import annotations
 
 import sys
 from pathlib import Path
-from types import SimpleNamespace
+from types import ModuleType, SimpleNamespace
 
 import torch
 from torch import nn
@@ -45,6 +46,24 @@ def reference():
 
     ns.joint = joint
     return ns, None
+
+
+def reference_graphs():
+    """The reference's ``WAMInfer.graphs`` (``CudaGraphForward``, graphs.py:30-128).
+    The module imports ``openwam``'s ``CausalConv3d`` for its VAE graph only; a
+    stand-in class under that module path lets it import without openwam.  Its
+    input guard is the reference's own C++ extension, built on first use by
+    ``graphs.extension()`` (torch.utils.cpp_extension, g++)."""
+    names = ["openwam", "openwam.model", "openwam.model.video_backbone", "openwam.model.video_backbone.wan",
+             "openwam.model.video_backbone.wan.models", "openwam.model.video_backbone.wan.models.vae"]
+    for name in names:
+        sys.modules.setdefault(name, ModuleType(name))
+    vae = sys.modules[names[-1]]
+    if not hasattr(vae, "CausalConv3d"):
+        vae.CausalConv3d = type("CausalConv3d", (nn.Conv3d,), {})
+    from WAMInfer import graphs
+
+    return graphs
 
 
 class _Attention(nn.Module):
@@ -155,19 +174,21 @@ class JointModel:
         mg = torch.Generator().manual_seed(seed + 2)
         self.mandatory = (torch.rand(TOKENS_PER_FRAME, generator=mg) < 0.05).to(device)
 
-    def states(self, reuse_count: int | None = None):
+    def states(self, reuse_count: int | None = None, video: torch.Tensor | None = None,
+               action: torch.Tensor | None = None):
         """Fresh video / action states of the request (the loop mutates them).
-        With reuse_count, token reuse with that capacity (runtime.py:244-246)."""
+        With reuse_count, token reuse with that capacity (runtime.py:244-246);
+        video / action replace the request's hidden states (used as they are)."""
         extras = {"_inference_context_kv": self.video_kv, "action_only": False, "record_first_frame": False}
         if reuse_count is not None:
             extras.update(token_reuse=dict(n=TOKENS_PER_FRAME, count=reuse_count, mandatory=self.mandatory,
                                            features=self.features, cache=self.history),
                           token_outputs=[])
         video = self.ref.blocks.VideoState(
-            hidden_states=self.video.clone(), time_mod=self.video_time, rope_freqs=self.video_rope,
+            hidden_states=self.video.clone() if video is None else video, time_mod=self.video_time, rope_freqs=self.video_rope,
             context_mask=self.context_mask, grid_frames=FRAMES, grid_height=12, grid_width=10, extras=extras)
         action = self.ref.blocks.ActionState(
-            x_action=self.action.clone(), t_mod=self.action_time, action_freqs=self.action_rope,
+            x_action=self.action.clone() if action is None else action, t_mod=self.action_time, action_freqs=self.action_rope,
             context_mask=self.context_mask, context_kv=self.action_kv)
         return video, action
 

@@ -217,3 +217,40 @@ def test_masked_block_skip_is_exact(cuda_device):
     out = masked_attention(q, k, v, none_kept, heads, False, 2)
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0  # every row fully masked: zeros, as SDPA
+
+
+def _fp64_attention(q, k, v, mask, heads):
+    import math
+
+    b, nq, hidden = q.shape
+    nk = k.shape[1]
+    qh, kh, vh = (t.double().view(b, t.shape[1], heads, 128).transpose(1, 2) for t in (q, k, v))
+    s = qh @ kh.transpose(-1, -2) / math.sqrt(128)
+    if mask is not None:
+        s = s.masked_fill(~torch.broadcast_to(mask, s.shape), -math.inf)
+    return (torch.softmax(s, -1).nan_to_num(0) @ vh).transpose(1, 2).reshape(b, nq, hidden)
+
+
+@pytest.mark.parametrize("nq,nk,mask_kind,tail", [(392, 392, None, False), (360, 512, "context", False),
+                                                   (32, 512, "context", True), (240, 513, "context", True)])
+def test_accuracy_against_fp64_matches_the_reference(cuda_device, nq, nk, mask_kind, tail):
+    """Distance from an fp64 softmax (no bf16 rounding anywhere), averaged over
+    four seeds on the DiT's shapes: this kernel (automatic key split) is no
+    further from it than the reference's Triton kernel, within 2 % (measured
+    on one B200: 2.07-2.11e-3 mean relative error against the reference's
+    2.09-2.11e-3; the bf16 rounding of the exact result alone is 1.41e-3)."""
+    from waminfer_b200.attention import masked_attention
+
+    triton = _reference_triton()
+    if triton is None:
+        pytest.skip("the reference's Triton kernel is unavailable")
+    ours_err = theirs_err = 0.0
+    for seed in range(4):
+        q, k, v, mask = _case(cuda_device, seed, 1, nq, nk, 24, mask_kind)
+        exact = _fp64_attention(q, k, v, mask, 24)
+        scale = float(exact.abs().mean())
+        ours_err += float((masked_attention(q, k, v, mask, 24, tail).double() - exact).abs().mean()) / scale
+        theirs_err += float((triton(q, k, v, mask, 24, tail=tail).double() - exact).abs().mean()) / scale
+    print("mean relative error vs fp64", (nq, nk, mask_kind), "ours %.4e reference %.4e" % (ours_err / 4,
+                                                                                          theirs_err / 4))
+    assert ours_err <= 1.02 * theirs_err
