@@ -97,7 +97,7 @@ struct AttnQSeg {
 struct AttnParams {
   const unsigned char* mask;  // bool, [b, h, q, k] through the strides below, or null (one segment each)
   long long mb, mh, mq, mk;   // mask strides in elements (0 = broadcast)
-  int skip_masked;            // mh == mq == 0: key blocks without a kept key are skipped
+  int skip_masked;            // mh == mq == 0: key blocks without a kept key are skipped (the kSkip kernel)
   AttnQSeg qseg[kAttnMaxQSeg];
   int nqseg;
   int krows[kAttnMaxKSeg];  // rows per batch of key segment t (map row = b * krows[t] + i)
@@ -167,6 +167,9 @@ __device__ __forceinline__ int attn_nth_active(const uint32_t* bits, int words, 
   return 0;  // not reached: n < the bitmap's population
 }
 
+// kSkip: the masked-block skip is compiled in (p.skip_masked set); the
+// instantiation without it carries none of its code or registers.
+template <bool kSkip>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     masked_attention_kernel(const __grid_constant__ AttnMaps maps, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -252,30 +255,47 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   pdl_wait_prior();
   if (threadIdx.x == 0) pdl_launch_dependents();
 
-  // Masked-block skip: which key blocks hold a kept key (one ballot per 32 keys).
-  if (p.skip_masked) {
-    if (threadIdx.x < kAttnSkipWords) skip_bits[threadIdx.x] = 0u;
-    __syncthreads();
+  // Masked-block skip: the TMA warp builds the bitmap of the key blocks that
+  // hold a kept key (lane l tests keys [16 l, 16 l + 16) of each 512-key
+  // round; lane 0 writes the words), so that its first lane can issue the
+  // first loads at once; the other warps read the bitmap after the
+  // block-wide barrier below.
+  if (kSkip && warp == kTmaWarp) {
     const int nk = kp.vis[0];  // the skip runs with one key segment
-    for (int k0 = warp * 32; k0 < nk; k0 += kAttnThreads) {
-      const int key = k0 + lane;
-      const bool kept = key < nk && p.mask[size_t(b) * p.mb + size_t(key) * p.mk] != 0;
-      if (__ballot_sync(0xffffffffu, kept) != 0u && lane == 0)
-        atomicOr(&skip_bits[(k0 / kAttnKeys) >> 5], 1u << ((k0 / kAttnKeys) & 31));
+    const unsigned char* mrow = p.mask + size_t(b) * p.mb;
+    const bool vec = p.mk == 1 && (reinterpret_cast<uintptr_t>(mrow) & 15u) == 0;
+    if (lane == 0)
+      for (int w = 0; w < skip_words; ++w) skip_bits[w] = 0u;
+    for (int base = 0; base < nk; base += 32 * 16) {
+      const int k0 = base + lane * 16;
+      bool kept = false;
+      if (vec && k0 + 16 <= nk) {
+        const uint4 m = *reinterpret_cast<const uint4*>(mrow + k0);
+        kept = (m.x | m.y | m.z | m.w) != 0u;
+      } else {
+        for (int i = 0; i < 16 && k0 + i < nk; ++i) kept |= mrow[size_t(k0 + i) * p.mk] != 0;
+      }
+      const uint32_t votes = __ballot_sync(0xffffffffu, kept);  // bit l: chunk l of the round
+      if (lane == 0)
+        for (int i = 0; i < 4; ++i) {  // 128-key block i of the round = chunks 8 i .. 8 i + 7
+          const int blk = base / kAttnKeys + i;
+          if (((votes >> (8 * i)) & 0xffu) != 0u) skip_bits[blk >> 5] |= 1u << (blk & 31);
+        }
     }
-    __syncthreads();
+    __syncwarp();
   }
-  int active = kp.total;
-  if (p.skip_masked) {
-    active = 0;
-    for (int w = 0; w < skip_words; ++w) active += __popc(skip_bits[w]);
-  }
-  // This CTA's share of the active key blocks: ordinals [jb, jb + nblocks).
-  const int jb = rank * active / split;
-  const int nblocks = (rank + 1) * active / split - jb;
-  auto block_at = [&](int j) {  // the key block of ordinal jb + j
-    const int o = jb + j;
-    return attn_block(kp, p.skip_masked ? attn_nth_active(skip_bits, skip_words, o) : o);
+  // Active key blocks (known to the TMA warp now, to every thread after the
+  // block-wide barrier) and the key block of an active ordinal.
+  auto count_active = [&]() {
+    int active = kp.total;
+    if (kSkip) {
+      active = 0;
+      for (int w = 0; w < skip_words; ++w) active += __popc(skip_bits[w]);
+    }
+    return active;
+  };
+  auto block_of = [&](int o) {
+    return attn_block(kp, kSkip ? attn_nth_active(skip_bits, skip_words, o) : o);
   };
 
   // TMA loads (issued by tma_lane only): Q once, K and V of block j into ring stage j & 1.
@@ -286,9 +306,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_load_2d(smem_addr(q_s + t * kAttnTile), &maps.q[seg], smem_addr(q_full), h * kAttnHeadDim + t * 64,
                   b * qs.map_batch_rows + qs.row0 + q0, keep);
   };
-  auto issue_kv = [&](int j) {
+  auto issue_kv = [&](int j, const AttnKeyBlock& kb) {  // ring stage j & 1
     const int s = j & 1;
-    const AttnKeyBlock kb = block_at(j);
     const int row = b * (kb.seg == 0 ? p.krows[0] : kb.seg == 1 ? p.krows[1] : p.krows[2]) + kb.row;
     uint8_t* st = kv_s + s * 4 * kAttnTile;
     // K and V rows of this block, dims [t*64, t*64+64) of the head, on separate barriers.
@@ -301,12 +320,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_load_2d(smem_addr(st + (2 + t) * kAttnTile), &maps.v[kb.seg], smem_addr(&v_full[s]),
                   h * kAttnHeadDim + t * 64, row, keep);
   };
-  // Without the skip the key blocks are known now: Q and the first two blocks
-  // go out before the block-wide barrier.
-  const int early = (!p.skip_masked && nblocks > 0) ? min(nblocks, 2) : 0;
-  if (tma_lane && early) {
-    issue_q();
-    for (int j = 0; j < early; ++j) issue_kv(j);
+  // Q and the first two key blocks go out before the block-wide barrier.
+  int early = 0;
+  if (tma_lane) {
+    const int active = count_active();
+    const int jb = rank * active / split;
+    early = min((rank + 1) * active / split - jb, 2);
+    if (early) issue_q();
+    for (int j = 0; j < early; ++j) issue_kv(j, block_of(jb + j));
   }
 
   // Optional phase trace (wamffn_trace_enable): {tag, start, first S ready,
@@ -322,7 +343,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         rec = g_trace + size_t(slot + 1) * kTraceWords;
         rec[0] = (unsigned long long)(blockIdx.x | (blockIdx.y << 16)) | (8ull << 32) | ((unsigned long long)rank << 48);
         rec[1] = globaltimer_ns();
-        rec[6] = smid() | ((unsigned long long)nblocks << 32);
         rec[7] = 0;
       }
     }
@@ -330,6 +350,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // This CTA's share of the active key blocks: ordinals [jb, jb + nblocks).
+  const int active = count_active();
+  const int jb = rank * active / split;
+  const int nblocks = (rank + 1) * active / split - jb;
+  if (rec && threadIdx.x == 0) rec[6] = smid() | ((unsigned long long)nblocks << 32);
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_s = tmem, tmem_o = tmem + kAttnKeys;
 
@@ -342,7 +367,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (j >= 2 && !wait_spin(smem_addr(&kv_empty[j & 1]), uint32_t((j >> 1) - 1) & 1u, abort_flag, p.status,
                                     WAMFFN_DEV_TIMEOUT))
           break;
-        issue_kv(j);
+        issue_kv(j, block_of(jb + j));
         issued = j + 1;
       }
       if (*abort_flag) {
@@ -449,7 +474,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       float sc[64];
       float bmax = -INFINITY;
-      const AttnKeyBlock kb = block_at(j);
+      const AttnKeyBlock kb = block_of(jb + j);
       const int k0 = kb.key + half * 64;             // first key of this half in the concatenation
       const int valid_keys = kb.valid - half * 64;   // keys past the segment are masked
       if (ok) {
@@ -664,48 +689,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int col = half * 64 + c * 32;
           if (col / W != rank) continue;  // warp-uniform
           const int off = col - rank * W;
-          uint32_t v[32];
-          __syncwarp();
-          if (has_o) {
-            tmem_ld32(tmem_o + lane_base + uint32_t(col), v);
-            tmem_wait_ld(v);
-          } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0u;
-          }
-          if (!row_live) continue;  // after the warp-wide load; nothing warp-wide follows in this iteration
-          float o[32], lsum = 0.f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = 0.f;
-          for (int k = 0; k < split; ++k) {  // rank order
-            const int slot = k < rank ? k : k - 1;
-            const float mk = k == rank ? m : slot_ml(slot)[0];
-            const float lk = k == rank ? lt : slot_ml(slot)[1];
-            const float f = ex2_approx(mk - safe);
-            lsum += lk * f;
-            if (k == rank) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] += __uint_as_float(v[i]) * f;
+          for (int hc = 0; hc < 2; ++hc) {  // 16 columns at a time: fewer live registers
+            const int c16 = col + hc * 16;
+            uint32_t v[16];
+            __syncwarp();
+            if (has_o) {
+              tmem_ld16(tmem_o + lane_base + uint32_t(c16), v);
+              tmem_wait_ld(v);
             } else {
-              const float4* src =
-                  reinterpret_cast<const float4*>(recv + slot * slot_bytes + kAttnRows * 8 + (r * pitch + off) * 4);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 x = src[i];
-                o[4 * i] += x.x * f;
-                o[4 * i + 1] += x.y * f;
-                o[4 * i + 2] += x.z * f;
-                o[4 * i + 3] += x.w * f;
-              }
+              for (int i = 0; i < 16; ++i) v[i] = 0u;
             }
-          }
-          const float inv = 1.0f / (lsum > 0.f ? lsum : 1.0f);
-          if (q < qs.rows) {
+            if (row_live) {
+              float o[16], lsum = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              *reinterpret_cast<uint4*>(orow + col + i) =
-                  make_uint4(bf2_pack(o[i] * inv, o[i + 1] * inv), bf2_pack(o[i + 2] * inv, o[i + 3] * inv),
-                             bf2_pack(o[i + 4] * inv, o[i + 5] * inv), bf2_pack(o[i + 6] * inv, o[i + 7] * inv));
+              for (int i = 0; i < 16; ++i) o[i] = 0.f;
+              for (int k = 0; k < split; ++k) {  // rank order
+                const int slot = k < rank ? k : k - 1;
+                const float mk = k == rank ? m : slot_ml(slot)[0];
+                const float lk = k == rank ? lt : slot_ml(slot)[1];
+                const float f = ex2_approx(mk - safe);
+                lsum += lk * f;
+                if (k == rank) {
+#pragma unroll
+                  for (int i = 0; i < 16; ++i) o[i] += __uint_as_float(v[i]) * f;
+                } else {
+                  const float4* src = reinterpret_cast<const float4*>(recv + slot * slot_bytes + kAttnRows * 8 +
+                                                                      (r * pitch + off + hc * 16) * 4);
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    const float4 x = src[i];
+                    o[4 * i] += x.x * f;
+                    o[4 * i + 1] += x.y * f;
+                    o[4 * i + 2] += x.z * f;
+                    o[4 * i + 3] += x.w * f;
+                  }
+                }
+              }
+              const float inv = 1.0f / (lsum > 0.f ? lsum : 1.0f);
+#pragma unroll
+              for (int i = 0; i < 16; i += 8)
+                *reinterpret_cast<uint4*>(orow + c16 + i) =
+                    make_uint4(bf2_pack(o[i] * inv, o[i + 1] * inv), bf2_pack(o[i + 2] * inv, o[i + 3] * inv),
+                               bf2_pack(o[i + 4] * inv, o[i + 5] * inv), bf2_pack(o[i + 6] * inv, o[i + 7] * inv));
+            }
           }
         }
       }

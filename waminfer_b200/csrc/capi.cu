@@ -155,7 +155,9 @@ int prepare_device(int device, int* sm_count) {
                                      kSmemLimit));
     WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemLimit));
-    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kAttnSmem));
+    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kAttnSmem));
     cudaFuncAttributes pass_attr{};
     WAMFFN_CUDA(cudaFuncGetAttributes(&pass_attr, stack_pass_kernel));  // its static barriers count too
@@ -1569,7 +1571,10 @@ int launch_attention(void* stream_, const AttnMaps& maps, AttnParams& p, int key
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel, maps, p));
+  if (p.skip_masked)
+    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel<true>, maps, p));
+  else
+    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel<false>, maps, p));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;
 }
