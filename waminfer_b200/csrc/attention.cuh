@@ -167,9 +167,10 @@ __device__ __forceinline__ int attn_nth_active(const uint32_t* bits, int words, 
   return 0;  // not reached: n < the bitmap's population
 }
 
-// kSkip: the masked-block skip is compiled in (p.skip_masked set); the
-// instantiation without it carries none of its code or registers.
-template <bool kSkip>
+// kSkip: the masked-block skip is compiled in (p.skip_masked set); kSplit:
+// the key-split combine is (p.split > 1).  An instantiation without a feature
+// carries none of its code or registers.
+template <bool kSkip, bool kSplit>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     masked_attention_kernel(const __grid_constant__ AttnMaps maps, const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint32_t* skip_bits = reinterpret_cast<uint32_t*>(xsum + 2 * kAttnRows);  // [kAttnSkipWords]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = p.split;
+  const int split = kSplit ? p.split : 1;
   const int ctile = int(blockIdx.x) / split, rank = int(blockIdx.x) - ctile * split;
   const int h = blockIdx.y, b = blockIdx.z;
   const int seg = (p.nqseg > 1 && ctile >= p.qseg[0].tiles) ? 1 : 0;

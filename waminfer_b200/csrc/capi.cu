@@ -155,10 +155,14 @@ int prepare_device(int device, int* sm_count) {
                                      kSmemLimit));
     WAMFFN_CUDA(cudaFuncSetAttribute(umma_gemm_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kSmemLimit));
-    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kAttnSmem));
-    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kAttnSmem));
+    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<false, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<false, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<true, false>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
+    WAMFFN_CUDA(cudaFuncSetAttribute(masked_attention_kernel<true, true>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem));
     cudaFuncAttributes pass_attr{};
     WAMFFN_CUDA(cudaFuncGetAttributes(&pass_attr, stack_pass_kernel));  // its static barriers count too
     WAMFFN_CUDA(cudaFuncSetAttribute(stack_pass_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1571,10 +1575,9 @@ int launch_attention(void* stream_, const AttnMaps& maps, AttnParams& p, int key
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (p.skip_masked)
-    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel<true>, maps, p));
-  else
-    WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, masked_attention_kernel<false>, maps, p));
+  auto kernel = p.skip_masked ? (split > 1 ? masked_attention_kernel<true, true> : masked_attention_kernel<true, false>)
+                              : (split > 1 ? masked_attention_kernel<false, true> : masked_attention_kernel<false, false>);
+  WAMFFN_CUDA(cudaLaunchKernelEx(&cfg, kernel, maps, p));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return WAMFFN_OK;
 }
