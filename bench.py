@@ -517,6 +517,41 @@ def reference_ffn_phase_ms(device, geo, weights, replays, lanes=1, ours_latency=
     return out
 
 
+def reference_geometry_timings(device, weights, stream, requests=8):
+    """One-lane request latency at the reference's own row semantics (the
+    runtime's token-reuse buckets, runtime.py:157-201): 360 video rows (3
+    latent frames of 120; the action rows run in the action branch, not in
+    the video FFN), update 0 with 32 / 64 / 96 refreshed current rows (272 /
+    304 / 336 FFN rows from layer 1), update 3 full.  Each bucket is timed in
+    alternation with the reference's FFN phase on the same geometry
+    (``reference_ffn_phase_ms``)."""
+    from waminfer_b200.stack import FFNStack, Geometry, Request
+
+    out = {}
+    for count in (32, 64, 96):
+        geo = Geometry(layers=len(weights), action=0, count=count)
+        stack = FFNStack(weights, geo, device, lanes=1)
+        reqs = [Request(geo, device, seed=77_000 + i) for i in range(requests)]
+        handle = stream.cuda_stream
+        with torch.cuda.stream(stream):
+            stack.enqueue_requests(reqs, handle, lanes=1)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            stack.enqueue_requests(reqs, handle, lanes=1)
+        ref = reference_ffn_phase_ms(device, geo, weights, replays=requests, lanes=1,
+                                     ours_latency=(graph, stream, requests))
+        graph.reset()
+        stack.close()
+        del stack, reqs
+        out[f"count_{count}"] = {
+            "rows_update0": geo.reuse_rows, "rows_update3": geo.seq,
+            "ours_latency_ms_per_request": ref.get("ours_latency_ms"),
+            "reference_ffn_phase_ms_per_request": ref["latency_ms"],
+            "speedup_vs_reference_ffn_phase": ref["latency_ms"] / ref["ours_latency_ms"]}
+    return out
+
+
 def norm_timings(device, geo, replays):
     """The modulated norm at S = 392 with per-token time rows,
     CROSS_RESIDUAL and FFN_RESIDUAL modes: this library's op against the
@@ -984,6 +1019,8 @@ def run_ours(args, world, rank, local):
                                   ours_latency=(paired_graph, stream, len(paired)),
                                   ours_lanes=(graph, stream, args.requests) if args.lanes > 1 else None)
         paired_graph.reset()
+        if "reference_ffn_phase_ms_per_request" in baselines:
+            baselines["reference_geometry"] = reference_geometry_timings(device, weights, stream)
         baselines["ours_ms_per_request"] = baselines.get("ours_paired_latency_ms_per_request", latency_ms)
         baselines["ours_lanes_ms_per_request"] = baselines.get("ours_paired_lanes_ms_per_request", ms_request)
         for key in ("torch_native", "reference_cublaslt"):
