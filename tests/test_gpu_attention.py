@@ -254,3 +254,30 @@ def test_accuracy_against_fp64_matches_the_reference(cuda_device, nq, nk, mask_k
     print("mean relative error vs fp64", (nq, nk, mask_kind), "ours %.4e reference %.4e" % (ours_err / 4,
                                                                                           theirs_err / 4))
     assert ours_err <= 1.02 * theirs_err
+
+
+@pytest.mark.parametrize("split", [0, 1, 2, 4])
+def test_per_batch_padding_masks_with_skip_and_split(cuda_device, split):
+    """Three batches with their own padded prompt lengths (the mask shared by
+    heads and queries, so fully masked key blocks are skipped per batch), a
+    fourth batch with no kept key at all, and the same masks as a strided
+    view (every other byte of a wider tensor: the per-key scalar path), at
+    every key split, against the oracle."""
+    from waminfer_b200.attention import masked_attention
+
+    g = torch.Generator(device=cuda_device).manual_seed(31)
+    b, nq, nk, heads = 4, 150, 600, 3
+    q, k, v = (torch.randn(b, n, heads * 128, device=cuda_device, generator=g).bfloat16() for n in (nq, nk, nk))
+    keep = torch.zeros(b, nk, dtype=torch.bool, device=cuda_device)
+    for i, length in enumerate((600, 300, 129, 0)):
+        keep[i, :length] = True
+    dense = keep.view(b, 1, 1, nk)
+    wide = torch.zeros(b, 1, 1, 2 * nk, dtype=torch.bool, device=cuda_device)
+    wide[..., ::2] = dense
+    ref = oattn.masked_attention(q, k, v, dense, heads)
+    for mask in (dense, wide[..., ::2]):
+        out = masked_attention(q, k, v, mask, heads, False, split)
+        torch.cuda.synchronize()
+        ok, msg = offn.check_close(out, ref)
+        assert ok, (split, mask.stride(), msg)
+        assert torch.count_nonzero(out[3]) == 0  # nothing kept: zeros
