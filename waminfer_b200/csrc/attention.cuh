@@ -27,7 +27,8 @@
 // One CTA per (128-query tile, head, batch); head dim D = 128.  Key blocks
 // stream through a 2-stage TMA ring (K and V rows as they lie in memory,
 // 128-byte swizzle; K is the K-major operand of Q K^T, V the MN-major operand
-// of P V).  Per key block:
+// of P V); a stage's K is refilled as soon as its S is done, its V once its
+// P V is done, so that the next blocks' K is resident before it is needed.  Per key block:
 //   warp 9 (one elected lane): S = Q K^T -> TMEM columns [0, 128)   (M = 128 queries, N = 128 keys)
 //   warps 0-7 (two per TMEM lane quarter: thread = query row x key half):
 //              read S, mask, row maximum (exchanged between the halves), exp2,
@@ -182,13 +183,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;    // [2]  K of a stage landed (S needs only K)
   uint64_t* v_full = bars + 3;    // [2]  V of a stage landed
-  uint64_t* kv_empty = bars + 5;  // [2]
-  uint64_t* s_full = bars + 7;
-  uint64_t* s_free = bars + 8;
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint64_t* xch_full = bars + 11;  // key-split combine: the peers' slots have landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* k_empty = bars + 5;   // [2]  S of the stage's block is done: its K may be overwritten
+  uint64_t* v_empty = bars + 7;   // [2]  P V of the stage's block is done: its V may be overwritten
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 10;
+  uint64_t* p_full = bars + 11;
+  uint64_t* o_done = bars + 12;
+  uint64_t* xch_full = bars + 13;  // key-split combine: the peers' slots have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* xmax = reinterpret_cast<float*>(smem + 12 * kAttnTile + 256);  // [2 halves][128 rows]
   float* xsum = xmax + 2 * kAttnRows;                                     // [2 halves][128 rows]
@@ -231,7 +233,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_addr(&k_full[s]), 1);
       mbar_init(smem_addr(&v_full[s]), 1);
-      mbar_init(smem_addr(&kv_empty[s]), 1);
+      mbar_init(smem_addr(&k_empty[s]), 1);
+      mbar_init(smem_addr(&v_empty[s]), 1);
     }
     mbar_init(smem_addr(s_full), 1);
     mbar_init(smem_addr(s_free), kAttnSoftmaxWarps);  // one arrival per softmax warp
@@ -307,19 +310,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tma_load_2d(smem_addr(q_s + t * kAttnTile), &maps.q[seg], smem_addr(q_full), h * kAttnHeadDim + t * 64,
                   b * qs.map_batch_rows + qs.row0 + q0, keep);
   };
-  auto issue_kv = [&](int j, const AttnKeyBlock& kb) {  // ring stage j & 1
+  // K and V rows of block j, dims [t*64, t*64+64) of the head, into ring
+  // stage j & 1 on separate barriers (S needs only K; K is free again once
+  // S is done, V only once P V is done).
+  auto kv_row = [&](const AttnKeyBlock& kb) {
+    return b * (kb.seg == 0 ? p.krows[0] : kb.seg == 1 ? p.krows[1] : p.krows[2]) + kb.row;
+  };
+  auto issue_k = [&](int j, const AttnKeyBlock& kb) {
     const int s = j & 1;
-    const int row = b * (kb.seg == 0 ? p.krows[0] : kb.seg == 1 ? p.krows[1] : p.krows[2]) + kb.row;
     uint8_t* st = kv_s + s * 4 * kAttnTile;
-    // K and V rows of this block, dims [t*64, t*64+64) of the head, on separate barriers.
     mbar_arrive_expect_tx(smem_addr(&k_full[s]), 2 * kAttnTile);
     for (int t = 0; t < 2; ++t)
       tma_load_2d(smem_addr(st + t * kAttnTile), &maps.k[kb.seg], smem_addr(&k_full[s]), h * kAttnHeadDim + t * 64,
-                  row, keep);
+                  kv_row(kb), keep);
+  };
+  auto issue_v = [&](int j, const AttnKeyBlock& kb) {
+    const int s = j & 1;
+    uint8_t* st = kv_s + s * 4 * kAttnTile;
     mbar_arrive_expect_tx(smem_addr(&v_full[s]), 2 * kAttnTile);
     for (int t = 0; t < 2; ++t)
       tma_load_2d(smem_addr(st + (2 + t) * kAttnTile), &maps.v[kb.seg], smem_addr(&v_full[s]),
-                  h * kAttnHeadDim + t * 64, row, keep);
+                  h * kAttnHeadDim + t * 64, kv_row(kb), keep);
   };
   // Q and the first two key blocks go out before the block-wide barrier.
   int early = 0;
@@ -328,7 +339,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int jb = rank * active / split;
     early = min((rank + 1) * active / split - jb, 2);
     if (early) issue_q();
-    for (int j = 0; j < early; ++j) issue_kv(j, block_of(jb + j));
+    for (int j = 0; j < early; ++j) {
+      const AttnKeyBlock kb = block_of(jb + j);
+      issue_k(j, kb);
+      issue_v(j, kb);
+    }
   }
 
   // Optional phase trace (wamffn_trace_enable): {tag, start, first S ready,
@@ -363,21 +378,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------ TMA loads
     if (nblocks > 0 && lane == 0) {
       if (!early) issue_q();
-      int issued = early;
+      int issued_k = early, issued_v = early;
       for (int j = early; j < nblocks; ++j) {
-        if (j >= 2 && !wait_spin(smem_addr(&kv_empty[j & 1]), uint32_t((j >> 1) - 1) & 1u, abort_flag, p.status,
-                                    WAMFFN_DEV_TIMEOUT))
-          break;
-        issue_kv(j, block_of(jb + j));
-        issued = j + 1;
+        const AttnKeyBlock kb = block_of(jb + j);
+        const uint32_t parity = uint32_t((j >> 1) - 1) & 1u;  // j >= 2 here
+        if (!wait_spin(smem_addr(&k_empty[j & 1]), parity, abort_flag, p.status, WAMFFN_DEV_TIMEOUT)) break;
+        issue_k(j, kb);
+        issued_k = j + 1;
+        if (!wait_spin(smem_addr(&v_empty[j & 1]), parity, abort_flag, p.status, WAMFFN_DEV_TIMEOUT)) break;
+        issue_v(j, kb);
+        issued_v = j + 1;
       }
       if (*abort_flag) {
         // Let the copies still in flight land before the CTA gives up its shared memory.
         wait_drain(smem_addr(q_full), 0u);
-        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
+        for (int j = issued_k > 2 ? issued_k - 2 : 0; j < issued_k; ++j)
           wait_drain(smem_addr(&k_full[j & 1]), uint32_t(j >> 1) & 1u);
+        for (int j = issued_v > 2 ? issued_v - 2 : 0; j < issued_v; ++j)
           wait_drain(smem_addr(&v_full[j & 1]), uint32_t(j >> 1) & 1u);
-        }
       }
     }
     __syncwarp();
@@ -403,6 +421,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             umma_bf16(tmem_s, umma_desc_sw128(smem_addr(q_s) + t * kAttnTile) + 2 * k,
                       umma_desc_sw128(st + t * kAttnTile) + 2 * k, idesc_s, (t | k) ? 1u : 0u);
         umma_commit(smem_addr(s_full));
+        umma_commit(smem_addr(&k_empty[j & 1]));
       }
       __syncwarp();
     };
@@ -444,7 +463,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     umma_desc_sw128_mn(st + 2 * kAttnTile + uint32_t(k) * 2 * kVGroupBytes, kVHalfBytes, kVGroupBytes),
                     idesc_o, (j | k) ? 1u : 0u);
         umma_commit(smem_addr(o_done));
-        umma_commit(smem_addr(&kv_empty[j & 1]));
+        umma_commit(smem_addr(&v_empty[j & 1]));
       }
       __syncwarp();
     }
