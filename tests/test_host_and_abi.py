@@ -184,3 +184,37 @@ def test_attention_abi_rejects_before_launching():
     args.key_split = 3  # the key split is 1, 2 or 4 CTAs (0: automatic)
     assert lib.wamffn_masked_attention(None, ctypes.byref(args)) == 1
     assert b"key_split" in lib.wamffn_last_error()
+
+
+def test_structured_attention_abi_rejects_before_launching():
+    """Argument checks of wamffn_joint_first_frame_attention and
+    wamffn_current_frame_attention run on the host, before any device call."""
+    import ctypes
+
+    from waminfer_b200 import _lib
+
+    lib = _lib.lib()
+    fake = 256
+    view = lambda rows: _lib.RowsView(data=fake, row_stride=3072, batch_stride=3072 * rows)  # noqa: E731
+    joint = _lib.JointAttentionArgs(q=view(392), k=view(392), v=view(392), out=fake, batch=1, count=392, video=360,
+                                    first=393, heads=24, head_dim=128)
+    assert lib.wamffn_joint_first_frame_attention(None, ctypes.byref(joint)) == 1  # first > count
+    assert b"first" in lib.wamffn_last_error()
+    joint.first, joint.head_dim = 120, 64
+    assert lib.wamffn_joint_first_frame_attention(None, ctypes.byref(joint)) == 3  # head_dim 64: unsupported
+    joint.head_dim, joint.k = 128, _lib.RowsView(data=fake + 2, row_stride=3072, batch_stride=3072 * 392)
+    assert lib.wamffn_joint_first_frame_attention(None, ctypes.byref(joint)) == 1  # k not 16-byte aligned
+    assert b"aligned" in lib.wamffn_last_error()
+
+    cur = _lib.CurrentFrameArgs(qv=view(240), qa=view(32), ck=view(120), kv=view(240), ka=view(32), cv=view(120),
+                                vv=view(240), va=view(32), ov=fake, oa=fake, batch=1, nc=120, nv=0, na=0, heads=24,
+                                head_dim=128)
+    assert lib.wamffn_current_frame_attention(None, ctypes.byref(cur)) == 1  # no query rows
+    cur.nv, cur.na, cur.key_split = 240, 32, 3
+    assert lib.wamffn_current_frame_attention(None, ctypes.byref(cur)) == 1  # key split 3
+    assert b"key_split" in lib.wamffn_last_error()
+    cur.key_split, cur.oa = 0, None
+    assert lib.wamffn_current_frame_attention(None, ctypes.byref(cur)) == 1  # action output missing
+    cur.oa, cur.vv = fake, _lib.RowsView(data=fake, row_stride=3072, batch_stride=3072 * 239)
+    assert lib.wamffn_current_frame_attention(None, ctypes.byref(cur)) == 1  # vv rows not at one stride
+    assert b"vv strides" in lib.wamffn_last_error()
