@@ -707,7 +707,7 @@ def projection_timings(device, geo, replays):
         t_torch = _graph_ms_per_replay(torch_linear, device, replays) / layers * 1e3
         flops = 2 * m * n * d
         out[name] = {"ours_us": t_ours, "torch_us": t_torch, "speedup": t_torch / t_ours,
-                     "ours_tflops": flops / (t_ours * 1e-6) / 1e12, "split_k": plan.selected_configuration()[4]}
+                     "ours_tflops": flops / (t_ours * 1e-6) / 1e12, **plan.layout()}
         plan.close()
         del ws, packed
     return out

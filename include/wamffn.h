@@ -109,8 +109,10 @@ int wamffn_trace_enable(int device, void* buffer, int records);
  * made by wamffn_pack_weight (the reference likewise runs on a repacked copy
  * made at prepare time, ffn.py:82-88); otherwise it is row-major [n_out, k_in].
  * fp32 accumulation, bf16 output.  Replaces Plan(...) (cpp:161-174).
- * `tune` != 0 times the candidate split-K factors on the device (like the
- * reference's exhaustive candidate timing, cpp:121-158) and keeps the fastest;
+ * `tune` != 0 times the candidate layouts (split-K factor x token groups)
+ * on the device, each over weight copies larger than L2 so that the weights
+ * stream from HBM as a model's per-layer weights do (like the reference's
+ * exhaustive candidate timing, cpp:121-158), and keeps the fastest;
  * otherwise a static heuristic picks the configuration.
  * ---------------------------------------------------------------------- */
 int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int flags, int tune,
@@ -123,11 +125,22 @@ int wamffn_linear_run(wamffn_linear_plan* plan, void* stream, const void* x, con
 
 /* Replaces Plan::selected_configuration (cpp:189).  Writes up to n values:
  * {feature_tile, token_pad, mma_count, stages, split_k, tmem_columns, tuned,
- *  streamk_groups}.  streamk_groups > 0: a GELU plan whose feature tiles
- * leave SMs idle runs as stream-K, its tiles' K blocks cut into that many
- * equal ranges, one per CTA pair on every SM, with a fixed-order fix-up of
- * the split tiles (deterministic). */
+ *  streamk_groups, token_groups}.  streamk_groups > 0: a GELU plan whose
+ * feature tiles leave SMs idle runs as stream-K, its tiles' K blocks cut into
+ * that many equal ranges, one per CTA pair on every SM, with a fixed-order
+ * fix-up of the split tiles (deterministic).  token_groups > 1: the rows are
+ * cut into that many equal groups, each with its own CTAs (token_pad is then
+ * per group). */
 int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values, int n);
+
+/* Sets a plan's layout explicitly: K split into `splits` (1..16; 1 for a GELU
+ * plan) slices whose fp32 partials a second kernel sums in split order, and
+ * the rows cut into `groups` (1..4) token groups.  No counterpart in the
+ * reference (cuBLASLt's algorithm choice is internal to Plan::tune,
+ * cpp:121-174); the tuner of wamffn_linear_plan_create picks among the same
+ * layouts.  Reallocates the split-K workspace when `splits` changes;
+ * synchronises the device; refused during CUDA Graph capture. */
+int wamffn_linear_plan_set_layout(wamffn_linear_plan* plan, int splits, int groups);
 
 /* Reads (and with clear != 0 resets) the device status word of a plan.
  * Synchronises the device. */

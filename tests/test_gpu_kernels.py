@@ -104,6 +104,54 @@ def test_down_projection_split_k(cuda_device, weights, packed, rows, layout):
     plan.close()
 
 
+@pytest.mark.parametrize("rows,n_out", [(392, 3072), (392, 9216), (304, 3072), (100, 3072), (17, 640), (513 - 1, 384)])
+def test_linear_layouts_split_k_and_token_groups(cuda_device, rows, n_out):
+    """Every layout the tuner may pick -- split-K x token groups (grid.z) --
+    against the fp32 oracle, for the attention projections' shapes (d x d and
+    the packed QKV 3d x d at the DiT's row counts) and odd ones; one bf16
+    rounding of the same fp32 sum, so the layouts agree with each other
+    within one bf16 ulp."""
+    from waminfer_b200.ffn import Plan, pack_weight
+
+    g = torch.Generator(device=cuda_device).manual_seed(rows * 7 + n_out)
+    x = randn((rows, D), cuda_device, g)
+    w = (torch.randn(n_out, D, device=cuda_device, generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(n_out, device=cuda_device, generator=g) * 0.01).to(torch.bfloat16)
+    ref = offn.bf16(x.float() @ w.float().T + bias.float())
+    pw = pack_weight(w)
+    plan = Plan(x, pw, bias, exhaustive=True, gelu=False)
+    tuned = plan.layout()
+    close(plan.run(x, pw, bias), ref, f"tuned {tuned}")
+    for split_k, groups in ((1, 1), (6, 1), (3, 2), (2, 3), (1, 2), (1, 4), (2, 2), (4, 1)):
+        if (rows + groups - 1) // groups > 512:
+            continue
+        plan.set_layout(split_k, groups)
+        assert plan.layout() == {"split_k": split_k, "token_groups": groups, "streamk_groups": 0}
+        out = plan.run(x, pw, bias)
+        close(out, ref, f"split_k={split_k} groups={groups}")
+        assert plan.status() == 0
+    plan.close()
+
+
+@pytest.mark.parametrize("rows", [100, 300, 392])
+def test_gelu_plan_token_groups(cuda_device, weights, packed, rows):
+    """The GELU epilogue with the rows cut into token groups (no split-K)."""
+    from waminfer_b200.ffn import Plan
+
+    x = randn((rows, D), cuda_device, weights["gen"])
+    ref = offn.bf16(offn.gelu_tanh(x.float() @ weights["w_up"].float().T + weights["b_up"].float()))
+    plan = Plan(x, packed["w_up"], weights["b_up"], exhaustive=False, gelu=True)
+    for groups in (2, 3, 4):
+        plan.set_layout(1, groups)
+        close(plan.run(x, packed["w_up"], weights["b_up"]), ref, f"groups={groups}")
+        assert plan.status() == 0
+    with pytest.raises(RuntimeError, match="never splits K"):
+        plan.set_layout(2, 1)
+    with pytest.raises(RuntimeError, match="groups=5"):
+        plan.set_layout(1, 5)
+    plan.close()
+
+
 @pytest.mark.parametrize("gelu", [False, True])
 @pytest.mark.parametrize("rows,n_out,k_in", [(1, 384, 256), (100, 384, 1024), (300, 640, 512), (512, 128, 3072)])
 def test_single_cta_tiles(cuda_device, rows, n_out, k_in, gelu):

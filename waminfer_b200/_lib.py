@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "wamffn_linear_plan_destroy",
     "wamffn_linear_run",
     "wamffn_linear_configuration",
+    "wamffn_linear_plan_set_layout",
     "wamffn_linear_status",
     "wamffn_linear_run_static",
     "wamffn_selftest_wait_timeout",
@@ -263,6 +264,7 @@ def _declare(lib):
     lib.wamffn_linear_plan_destroy.argtypes = [vp]
     lib.wamffn_linear_run.argtypes = [vp, vp, vp, vp, vp, vp]
     lib.wamffn_linear_configuration.argtypes = [vp, u32p, i]
+    lib.wamffn_linear_plan_set_layout.argtypes = [vp, i, i]
     lib.wamffn_linear_status.argtypes = [vp, u32p, i]
     lib.wamffn_linear_run_static.argtypes = [i, vp, i, i, i, i, i, vp, vp, vp, vp, vp]
     lib.wamffn_selftest_wait_timeout.argtypes = [vp, vp, ctypes.c_int64]

@@ -230,6 +230,8 @@ int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, i
   rows = (rows + groups - 1) / groups;  // rows per token group
   if (rows > kMaxTokens)
     return fail(WAMFFN_ERR_UNSUPPORTED, "rows per token group=%d above %d", rows, kMaxTokens);
+  if ((groups - 1) * rows >= total_rows)
+    return fail(WAMFFN_ERR_UNSUPPORTED, "%d rows leave token group %d of %d empty", total_rows, groups - 1, groups);
   if (n_out < kFeatTile || n_out % kFeatTile)
     return fail(WAMFFN_ERR_UNSUPPORTED, "n_out=%d must be a positive multiple of %d", n_out, kFeatTile);
   if (k_in < kBlockK || k_in % kBlockK)
@@ -483,18 +485,22 @@ int linear_execute(wamffn_linear_plan* plan, cudaStream_t stream, const void* x,
 }
 
 // Times `iters` launches of the plan on scratch operands; returns ms per launch.
-int time_linear(wamffn_linear_plan* plan, const void* x, const void* w, const void* b, void* out,
-                float* ms) {
+// The launches rotate over `copies` weight matrices of w_bytes each (together
+// larger than L2), so that every launch streams its weights from HBM, as the
+// per-layer weights of a model do.
+int time_linear(wamffn_linear_plan* plan, const void* x, const void* w, size_t w_bytes, int copies,
+                const void* b, void* out, float* ms) {
   cudaStream_t s;
   WAMFFN_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
   cudaEvent_t e0, e1;
   WAMFFN_CUDA(cudaEventCreate(&e0));
   WAMFFN_CUDA(cudaEventCreate(&e1));
+  auto weight = [&](int i) { return static_cast<const void*>(static_cast<const char*>(w) + (i % copies) * w_bytes); };
   int rc = WAMFFN_OK;
-  for (int i = 0; i < 3 && !rc; ++i) rc = linear_execute(plan, s, x, w, b, out);
+  for (int i = 0; i < 3 && !rc; ++i) rc = linear_execute(plan, s, x, weight(i), b, out);
   const int iters = 16;
   if (!rc) WAMFFN_CUDA(cudaEventRecord(e0, s));
-  for (int i = 0; i < iters && !rc; ++i) rc = linear_execute(plan, s, x, w, b, out);
+  for (int i = 0; i < iters && !rc; ++i) rc = linear_execute(plan, s, x, weight(3 + i), b, out);
   if (!rc) {
     WAMFFN_CUDA(cudaEventRecord(e1, s));
     WAMFFN_CUDA(cudaEventSynchronize(e1));
@@ -568,40 +574,54 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
     return cleanup(fail(WAMFFN_ERR_CUDA, "stream-K workspace allocation failed"));
   const int tiles = n_out / kFeatTile;
   if (tune) {
-    // Candidate split-K factors are timed on scratch operands, the way the
-    // reference times every candidate algorithm (cpp:121-158).
+    // Candidate layouts -- split-K factor x token groups (grid.z), and for a
+    // GELU plan the stream-K grid -- are timed on scratch operands, the way
+    // the reference times every candidate algorithm (cpp:121-158).  Split-K
+    // moves fp32 partials through L2; token groups re-read each weight tile
+    // (from L2 after the first group) but write no partials.
     int max_s = 1;
     for (int s = 2; !plan->gelu && s <= 16 && tiles * s <= 2 * sm && (k_in / kBlockK) / s >= 4; ++s) max_s = s;
+    const size_t w_bytes = size_t(n_out) * k_in * 2;
+    // Enough weight copies to exceed L2 (at most 16 and 192 MB).
+    int copies = int((size_t(160) << 20) / w_bytes) + 1;
+    if (copies > 16) copies = 16;
+    while (copies > 1 && copies * w_bytes > (size_t(192) << 20)) --copies;
     void *x = nullptr, *w = nullptr, *b = nullptr, *o = nullptr;
     bool okalloc = cudaMalloc(&x, size_t(rows) * k_in * 2) == cudaSuccess &&
-                   cudaMalloc(&w, size_t(n_out) * k_in * 2) == cudaSuccess &&
+                   cudaMalloc(&w, copies * w_bytes) == cudaSuccess &&
                    cudaMalloc(&b, size_t(n_out) * 2) == cudaSuccess &&
                    cudaMalloc(&o, size_t(rows) * n_out * 2) == cudaSuccess &&
                    (max_s == 1 || cudaMalloc(&plan->partial, size_t(max_s) * rows * n_out * 4) == cudaSuccess);
     if (okalloc) {
       cudaMemset(x, 0x3c, size_t(rows) * k_in * 2);
-      cudaMemset(w, 0x3c, size_t(n_out) * k_in * 2);
+      cudaMemset(w, 0x3c, copies * w_bytes);
       cudaMemset(b, 0, size_t(n_out) * 2);
       float best = 1e30f;
-      int best_s = plan->cfg.splits, best_sk = 0;
+      int best_s = plan->cfg.splits, best_g = 1, best_sk = 0;
       for (int s = 1; s <= max_s; ++s) {
-        // Candidates: split-K factors, and for the GELU plan also the stream-K grid.
-        const int sks[2] = {0, sk_candidate};
-        const int n_sk = (s == 1 && sk_candidate > 0) ? 2 : 1;
-        for (int j = 0; j < n_sk; ++j) {
-          GemmConfig c;
-          if (make_gemm_config(rows, n_out, k_in, s, &c)) continue;
-          c.sk = sks[j];
-          plan->cfg = c;
-          float ms = 0;
-          if (time_linear(plan, x, w, b, o, &ms) == WAMFFN_OK && ms < best) {
-            best = ms;
-            best_s = s;
-            best_sk = sks[j];
+        for (int g = 1; g <= 4; ++g) {
+          if (g > 1 && (tiles * s * g > sm || (rows + g - 1) / g < 16)) break;
+          // Candidates: split-K factors x token groups, and for the GELU plan
+          // also the stream-K grid.
+          const int sks[2] = {0, sk_candidate};
+          const int n_sk = (s == 1 && g == 1 && sk_candidate > 0) ? 2 : 1;
+          for (int j = 0; j < n_sk; ++j) {
+            GemmConfig c;
+            if (make_gemm_config(rows, n_out, k_in, s, &c, g)) continue;
+            if (c.splits != s) continue;
+            c.sk = sks[j];
+            plan->cfg = c;
+            float ms = 0;
+            if (time_linear(plan, x, w, w_bytes, copies, b, o, &ms) == WAMFFN_OK && ms < best) {
+              best = ms;
+              best_s = s;
+              best_g = g;
+              best_sk = sks[j];
+            }
           }
         }
       }
-      make_gemm_config(rows, n_out, k_in, best_s, &plan->cfg);
+      make_gemm_config(rows, n_out, k_in, best_s, &plan->cfg, best_g);
       plan->cfg.sk = best_sk;
       plan->tuned = 1;
     }
@@ -652,6 +672,41 @@ int wamffn_linear_configuration(const wamffn_linear_plan* plan, uint32_t* values
                          uint32_t(plan->tuned)};
   for (int i = 0; i < n && i < 7; ++i) values[i] = v[i];
   if (n > 7) values[7] = uint32_t(c.sk);  // stream-K CTA groups (0 = data-parallel grid)
+  if (n > 8) values[8] = uint32_t(c.groups);  // token groups (grid.z)
+  return WAMFFN_OK;
+}
+
+int wamffn_linear_plan_set_layout(wamffn_linear_plan* plan, int splits, int groups) {
+  if (!plan) return fail(WAMFFN_ERR_INVALID, "plan is null");
+  if (splits < 1 || splits > 16) return fail(WAMFFN_ERR_INVALID, "splits=%d outside [1, 16]", splits);
+  if (groups < 1 || groups > 4) return fail(WAMFFN_ERR_INVALID, "groups=%d outside [1, 4]", groups);
+  if (plan->gelu && splits != 1)
+    return fail(WAMFFN_ERR_INVALID, "a GELU plan never splits K (the split-K reduction applies the bias only)");
+  DeviceGuard guard(plan->device);
+  if (!guard.ok) return fail(WAMFFN_ERR_CUDA, "cannot select device %d", plan->device);
+  {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    WAMFFN_CUDA(cudaStreamIsCapturing(cudaStreamLegacy, &st));
+    if (st != cudaStreamCaptureStatusNone)
+      return fail(WAMFFN_ERR_CAPTURE, "a plan's layout must be set before CUDA Graph capture");
+  }
+  GemmConfig c;
+  int rc = make_gemm_config(plan->cfg.rows, plan->cfg.n_out, plan->cfg.k_in, splits, &c, groups);
+  if (rc) return rc;
+  if (c.splits != splits)
+    return fail(WAMFFN_ERR_INVALID, "splits=%d exceeds the %d K blocks", splits, plan->cfg.k_in / kBlockK);
+  // Launches already enqueued may still read the old workspace.
+  WAMFFN_CUDA(cudaDeviceSynchronize());
+  if (splits != plan->cfg.splits) {
+    cudaFree(plan->partial);
+    plan->partial = nullptr;
+    if (splits > 1 &&
+        cudaMalloc(&plan->partial, size_t(splits) * c.rows * c.n_out * sizeof(float)) != cudaSuccess) {
+      make_gemm_config(c.rows, c.n_out, c.k_in, 1, &plan->cfg);  // a plan that still runs
+      return fail(WAMFFN_ERR_CUDA, "split-K workspace allocation failed");
+    }
+  }
+  plan->cfg = c;  // data-parallel grid (no stream-K)
   return WAMFFN_OK;
 }
 

@@ -118,6 +118,22 @@ class Plan:
         _lib.check(_lib.lib().wamffn_linear_configuration(self._handle, values, 7))
         return list(values)
 
+    def layout(self) -> dict:
+        """The GEMM layout the plan runs: split-K factor, token groups and
+        stream-K CTA groups (0: data-parallel grid)."""
+        values = (ctypes.c_uint32 * 9)()
+        _lib.check(_lib.lib().wamffn_linear_configuration(self._handle, values, 9))
+        return {"split_k": int(values[4]), "token_groups": int(values[8]), "streamk_groups": int(values[7])}
+
+    def set_layout(self, split_k: int, token_groups: int = 1) -> None:
+        """Overrides the tuner's choice (K split into ``split_k`` slices, rows
+        cut into ``token_groups`` groups); synchronises the device."""
+        if self._handle is None:
+            raise RuntimeError("plan is closed")
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("a plan's layout must be set before CUDA Graph capture")
+        _lib.check(_lib.lib().wamffn_linear_plan_set_layout(self._handle, int(split_k), int(token_groups)))
+
     def status(self, clear: bool = True) -> int:
         """Device status word (timeout / bad-index bits); synchronises the device."""
         value = ctypes.c_uint32()
