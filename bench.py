@@ -65,6 +65,9 @@ def parse():
                    help="profiling aid: time one component on cuda:0 and print its JSON (no bench line): the "
                         "modulated norm against the reference's Triton kernel, the attention projections against "
                         "torch, or the up-projection GEMM alone")
+    p.add_argument("--proj-layout", default=None, metavar="SxG",
+                   help="with --only projections: run every projection plan at split-K S x G token groups instead "
+                        "of the tuner's choice (a profiler's slowed timings would mislead the tuner)")
     p.add_argument("--tp", action="store_true",
                    help="tensor-parallel mode: every request's FFN hidden dimension split across the --gpus ranks "
                         "(one all-reduce per layer, strong scaling); not the default bench line")
@@ -675,7 +678,7 @@ def attention_timings(device, replays, heads=24):
     return out
 
 
-def projection_timings(device, geo, replays):
+def projection_timings(device, geo, replays, layout=None):
     """Attention-side projections of one block at M = 392 rows (packed QKV
     3072 -> 9216, self-attention output, cross-attention query and output,
     3072 -> 3072): this library's plans against torch's F.linear (cuBLAS, what
@@ -694,6 +697,8 @@ def projection_timings(device, geo, replays):
         b = (torch.randn(n, device=device, generator=g) * 0.01).to(torch.bfloat16)
         packed = [pack_weight(w) for w in ws]
         plan = Plan(x, packed[0], b, True, False)
+        if layout is not None:
+            plan.set_layout(*layout)
 
         def ours():
             for w in packed:
@@ -703,7 +708,9 @@ def projection_timings(device, geo, replays):
             for w in ws:
                 F.linear(x, w, b)
 
-        t_ours = _graph_ms_per_replay(ours, device, replays) / layers * 1e3
+        # NVTX range per projection: `ncu --nvtx --nvtx-include "ours_self_out/"` captures its launches.
+        with torch.cuda.nvtx.range(f"ours_{name}"):
+            t_ours = _graph_ms_per_replay(ours, device, replays) / layers * 1e3
         t_torch = _graph_ms_per_replay(torch_linear, device, replays) / layers * 1e3
         flops = 2 * m * n * d
         out[name] = {"ours_us": t_ours, "torch_us": t_torch, "speedup": t_torch / t_ours,
@@ -1180,7 +1187,8 @@ def run_only(args):
     elif args.only == "attention":
         out = attention_timings(device, 20)
     elif args.only == "projections":
-        out = projection_timings(device, geo, 20)
+        layout = tuple(int(v) for v in args.proj_layout.lower().split("x")) if args.proj_layout else None
+        out = projection_timings(device, geo, 20, layout)
     else:
         pk, kind = peaks()
         out = time_dominant_kernel(device, geo, pk)
