@@ -439,8 +439,10 @@ __global__ void __launch_bounds__(kNormRegThreads) modnorm_reg_kernel(const Norm
   }
 }
 
+constexpr int kEpiSplitsBatch = 3;  // split-K partials loaded per batch of independent loads
+
 // One CTA per sequence row.
-__global__ void __launch_bounds__(kRowThreads) rowepi_kernel(const EpiParams p) {
+__global__ void __launch_bounds__(kRowThreads, 3) rowepi_kernel(const EpiParams p) {
   const int row = blockIdx.x;
   const int tid = threadIdx.x;
   const int nvec = p.dim >> 3;
@@ -457,12 +459,25 @@ __global__ void __launch_bounds__(kRowThreads) rowepi_kernel(const EpiParams p) 
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int s = 0; s < p.splits; ++s) {
-        const float4* src =
-            reinterpret_cast<const float4*>(p.partial + (size_t(s) * p.m + j) * p.dim + e);
-        const float4 a = src[0], c = src[1];
-        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-        acc[4] += c.x; acc[5] += c.y; acc[6] += c.z; acc[7] += c.w;
+      // Partials in batches of independent loads, summed in split order.
+      for (int s0 = 0; s0 < p.splits; s0 += kEpiSplitsBatch) {
+        float4 part[kEpiSplitsBatch][2];
+#pragma unroll
+        for (int s = 0; s < kEpiSplitsBatch; ++s) {
+          if (s0 + s < p.splits) {
+            const float4* src =
+                reinterpret_cast<const float4*>(p.partial + (size_t(s0 + s) * p.m + j) * p.dim + e);
+            part[s][0] = src[0];
+            part[s][1] = src[1];
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < kEpiSplitsBatch; ++s) {
+          if (s0 + s < p.splits) {
+            acc[0] += part[s][0].x; acc[1] += part[s][0].y; acc[2] += part[s][0].z; acc[3] += part[s][0].w;
+            acc[4] += part[s][1].x; acc[5] += part[s][1].y; acc[6] += part[s][1].z; acc[7] += part[s][1].w;
+          }
+        }
       }
       float bb[8];
       load8(p.bias + e, bb);
