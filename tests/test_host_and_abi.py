@@ -40,6 +40,8 @@ def test_abi_rejects_bad_arguments_without_a_gpu():
     assert lib.wamffn_linear_plan_create(0, 16, 100, 64, 1, 0, ctypes.byref(out)) != 0   # n_out % 128
     assert b"n_out" in lib.wamffn_last_error()
     assert lib.wamffn_linear_run(None, None, None, None, None, None) == _lib.WAMFFN_ERR_INVALID
+    assert lib.wamffn_linear_plan_set_layout(None, 2, 1) == _lib.WAMFFN_ERR_INVALID
+    assert b"plan is null" in lib.wamffn_last_error()
     assert lib.wamffn_block_run(None, None, None) == _lib.WAMFFN_ERR_INVALID
     args = _lib.NormArgs(rows=4, dim=12, mode=0)
     assert lib.wamffn_modulated_norm(None, ctypes.byref(args)) == _lib.WAMFFN_ERR_INVALID
