@@ -587,8 +587,14 @@ int wamffn_linear_plan_create(int device, int rows, int n_out, int k_in, int fla
     if (copies > 16) copies = 16;
     while (copies > 1 && copies * w_bytes > (size_t(192) << 20)) --copies;
     void *x = nullptr, *w = nullptr, *b = nullptr, *o = nullptr;
+    // Short of memory for the copies: time on one (L2-resident) weight copy.
+    while (copies > 1 && cudaMalloc(&w, copies * w_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      w = nullptr;
+      copies = 1;
+    }
     bool okalloc = cudaMalloc(&x, size_t(rows) * k_in * 2) == cudaSuccess &&
-                   cudaMalloc(&w, copies * w_bytes) == cudaSuccess &&
+                   (w != nullptr || cudaMalloc(&w, copies * w_bytes) == cudaSuccess) &&
                    cudaMalloc(&b, size_t(n_out) * 2) == cudaSuccess &&
                    cudaMalloc(&o, size_t(rows) * n_out * 2) == cudaSuccess &&
                    (max_s == 1 || cudaMalloc(&plan->partial, size_t(max_s) * rows * n_out * 4) == cudaSuccess);
