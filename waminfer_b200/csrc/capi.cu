@@ -222,7 +222,7 @@ bool pair_enabled() {
 }
 
 int make_gemm_config(int rows, int n_out, int k_in, int splits, GemmConfig* c, int groups = 1,
-                     int smem_budget = kSmemLimit - kSmemReserve) {
+                     int smem_budget = kSmemLimit - kSmemReserve - kGemmRowSlack) {
   if (rows < 1 || rows > kMaxTokens * 4)
     return fail(WAMFFN_ERR_UNSUPPORTED, "rows=%d outside [1, %d]", rows, kMaxTokens * 4);
   if (groups < 1 || groups > 4) return fail(WAMFFN_ERR_UNSUPPORTED, "token groups=%d outside [1, 4]", groups);

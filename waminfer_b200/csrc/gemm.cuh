@@ -71,6 +71,11 @@ constexpr int kMaxAStages = 16;
 constexpr int kMaxBStages = 8;
 constexpr int kSmemLimit = 232448;     // 227 KB opt-in dynamic shared memory
 constexpr int kSmemReserve = 1024 + 512;  // alignment slack + barriers
+// Shared memory the GEMM's rings leave unused so that one row-kernel CTA (a
+// 3072-wide fp32 row, 12 KB, plus its own reservation) fits on the SM beside a
+// GEMM CTA: concurrent request lanes then run layer-boundary rows on the SMs
+// whose GEMM CTA is waiting on its tensor pipe.
+constexpr int kGemmRowSlack = 14 * 1024;
 
 struct GemmParams {
   int tokens;        // real activation rows (all token groups)
